@@ -1,0 +1,250 @@
+// q8_store.cu -- Q8_0 KV-store kernel for sm_100a.
+//
+// One warp per (token, kv-head) row.  Each lane loads 4 consecutive elements
+// with one 8-byte (16-bit types) or 16-byte (fp32) vector load, so a 32-
+// element Q8_0 block is spread over 8 lanes and its absmax needs three
+// butterfly shuffles.  The quantised row is assembled in shared memory and
+// written with the widest store the destination alignment allows (8 bytes
+// for the 136-byte rows of D = 128).
+//
+// Numerics follow the reference kernel exactly
+// (extension/gfx906_fa_quant.cu:51-84): fp32 absmax, d = amax / 127.0f
+// (IEEE division), id = d > 0 ? 1/d : 0 (IEEE reciprocal), q = rint(v * id)
+// (round half to even) clamped to [-128, 127], scale stored as fp16(d) with
+// round-to-nearest-even.  This translation unit is built without
+// --use_fast_math, so `/` is the correctly rounded division.
+//
+// The same kernel serves three callers:
+//   * dense quantisation (quantize_q8_0, gfx906_fa_quant.cu:100-129),
+//   * the paged K store by slot_mapping (reshape_and_cache_q8,
+//     gfx906_fa_quant.cu:150-200),
+//   * the fused K+V store that replaces vLLM's Triton reshape_and_cache
+//     (backend.py:416-425): V is either copied as 16-bit rows or quantised
+//     to Q8_0 with the same rules as K.
+#include "common.cuh"
+#include "gfx906_fa_b200.h"
+
+namespace g9 {
+
+struct StoreArgs {
+  const void* key;              // [T, Hkv, D], element strides below
+  const void* value;            // may be null (v_mode == 0)
+  const int64_t* slot_mapping;  // [T]; null -> slot = token index
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  int64_t key_tok, key_head;    // elements
+  int64_t val_tok, val_head;    // elements
+  int64_t kc_blk, kc_tok, kc_head;  // bytes
+  int64_t vc_blk, vc_tok, vc_head;  // bytes
+  int key_dt, val_dt;
+  int v_mode;                   // 0: no V, 1: copy 16-bit rows, 2: quantise to Q8_0
+  int T, Hkv, D, bs;
+  int k_store_w;                // widest aligned store for K rows (2, 4 or 8 bytes)
+  int v_store_w;                // same for V rows
+  int vec_ok_k, vec_ok_v;       // 1 when 4-element vector loads are aligned
+};
+
+constexpr int kWarps = 8;
+constexpr int kMaxD = 512;
+constexpr int kStage = ((kMaxD / QK) * QBLOCK + 7) & ~7;   // 544 bytes per warp
+
+// Quantise one row of D elements held as 4 elements per lane per 128-element
+// chunk and leave the Q8_0 bytes in `stage`.
+__device__ __forceinline__ void quant_row_to_stage(const void* src, int64_t base, int dt, int D,
+                                                   bool vec_ok, uint8_t* stage) {
+  const int lane = lane_id();
+  for (int c0 = 0; c0 < D; c0 += 128) {
+    const int e0 = c0 + 4 * lane;             // first element this lane owns
+    const bool active = e0 < D;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (active) {
+      if (vec_ok) {
+        load_four(src, base + e0, dt, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = load_one(src, base + e0 + i, dt);
+      }
+    }
+    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    const float d = amax / 127.0f;
+    const float id = d > 0.0f ? __frcp_rn(d) : 0.0f;
+    if (active) {
+      const int blk = e0 / QK;                 // block index within the row
+      const int j = (e0 % QK) / 4;             // lane slot within the block (0..7)
+      uint8_t* out = stage + blk * QBLOCK;
+      uint32_t packed = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int qi = __float2int_rn(v[i] * id);
+        qi = max(-128, min(127, qi));
+        packed |= (uint32_t)(qi & 0xff) << (8 * i);
+      }
+      // byte offset 2 + 4j is 2-aligned: two 16-bit stores
+      uint16_t* o16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * j);
+      o16[0] = (uint16_t)(packed & 0xffffu);
+      o16[1] = (uint16_t)(packed >> 16);
+      if (j == 0) {
+        __half dh = __float2half_rn(d);
+        *reinterpret_cast<uint16_t*>(out) = __half_as_ushort(dh);
+      }
+    }
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void stage_to_global(const uint8_t* stage, uint8_t* dst, int bytes, int w) {
+  const int lane = lane_id();
+  if (w == 8) {
+    for (int i = lane; i < bytes / 8; i += 32)
+      reinterpret_cast<uint64_t*>(dst)[i] = reinterpret_cast<const uint64_t*>(stage)[i];
+  } else if (w == 4) {
+    for (int i = lane; i < bytes / 4; i += 32)
+      reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(stage)[i];
+  } else {
+    for (int i = lane; i < bytes / 2; i += 32)
+      reinterpret_cast<uint16_t*>(dst)[i] = reinterpret_cast<const uint16_t*>(stage)[i];
+  }
+  __syncwarp();
+}
+
+__global__ void __launch_bounds__(kWarps * 32) q8_store_kernel(StoreArgs a) {
+  __shared__ __align__(16) uint8_t stage_all[kWarps][kStage];
+  uint8_t* stage = stage_all[warp_id()];
+  const int rb = q8_row_bytes(a.D);
+  const int64_t rows = (int64_t)a.T * a.Hkv;
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp_id(); row < rows;
+       row += (int64_t)gridDim.x * kWarps) {
+    const int t = (int)(row / a.Hkv);
+    const int h = (int)(row % a.Hkv);
+    const int64_t slot = a.slot_mapping ? a.slot_mapping[t] : (int64_t)t;
+    if (slot < 0) continue;                              // padded token
+    const int64_t blk = slot / a.bs, off = slot % a.bs;
+    // ---- K: quantise -------------------------------------------------------
+    quant_row_to_stage(a.key, (int64_t)t * a.key_tok + (int64_t)h * a.key_head, a.key_dt, a.D,
+                       a.vec_ok_k, stage);
+    stage_to_global(stage, a.k_cache + blk * a.kc_blk + off * a.kc_tok + h * a.kc_head, rb,
+                    a.k_store_w);
+    // ---- V -----------------------------------------------------------------
+    if (a.v_mode == 2) {
+      quant_row_to_stage(a.value, (int64_t)t * a.val_tok + (int64_t)h * a.val_head, a.val_dt, a.D,
+                         a.vec_ok_v, stage);
+      stage_to_global(stage, a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head, rb,
+                      a.v_store_w);
+    } else if (a.v_mode == 1) {
+      const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) +
+                            (int64_t)t * a.val_tok + (int64_t)h * a.val_head;
+      uint8_t* dst = a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head;
+      const int lane = lane_id();
+      if (a.v_store_w == 8 && a.vec_ok_v) {
+        for (int i = lane; i < a.D / 4; i += 32)
+          reinterpret_cast<uint2*>(dst)[i] = reinterpret_cast<const uint2*>(src)[i];
+      } else {
+        for (int i = lane; i < a.D; i += 32)
+          reinterpret_cast<uint16_t*>(dst)[i] = src[i];
+      }
+    }
+  }
+}
+
+static int store_width(const void* base, int64_t a, int64_t b, int64_t c, int row_bytes) {
+  uintptr_t m = (uintptr_t)base | (uintptr_t)a | (uintptr_t)b | (uintptr_t)c | (uintptr_t)row_bytes;
+  if ((m & 7) == 0) return 8;
+  if ((m & 3) == 0) return 4;
+  return 2;
+}
+
+static bool vec_aligned(const void* base, int dt, int64_t s0, int64_t s1) {
+  const int esz = dt == DT_F32 ? 4 : 2;
+  const uintptr_t align = dt == DT_F32 ? 16 : 8;
+  return ((uintptr_t)base % align) == 0 && (s0 % 4) == 0 && (s1 % 4) == 0 && esz > 0;
+}
+
+static int grid_for_rows(int64_t rows) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int64_t want = (rows + kWarps - 1) / kWarps;
+  int64_t cap = (int64_t)sms * 16;               // grid-stride beyond 16 CTAs per SM
+  return (int)(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+cudaError_t launch_store(const StoreArgs& a, cudaStream_t stream) {
+  const int64_t rows = (int64_t)a.T * a.Hkv;
+  if (rows == 0) return cudaSuccess;
+  q8_store_kernel<<<grid_for_rows(rows), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace g9
+
+G9_ERROR_ACCESSORS(store)
+
+using namespace g9;
+
+extern "C" cudaError_t launch_quantize_q8_0_dense(const void* x, uint8_t* y, int N, int D,
+                                                  cudaStream_t stream) {
+  return gfx906_fa_quantize_q8_0(x, G9_DT_F16, y, (int64_t)N, D, stream);
+}
+
+extern "C" cudaError_t gfx906_fa_quantize_q8_0(const void* x, int x_dtype, uint8_t* y, int64_t N,
+                                               int D, cudaStream_t stream) {
+  if (D % QK != 0 || D <= 0 || D > kMaxD || N < 0 || x_dtype < 0 || x_dtype > 2) return cudaErrorInvalidValue;
+  if (N == 0) return cudaSuccess;
+  if (N > INT32_MAX) return cudaErrorInvalidValue;
+  StoreArgs a{};
+  const int rb = q8_row_bytes(D);
+  a.key = x; a.key_dt = x_dtype; a.key_tok = D; a.key_head = 0;
+  a.k_cache = y; a.kc_blk = rb; a.kc_tok = 0; a.kc_head = 0;
+  a.T = (int)N; a.Hkv = 1; a.D = D; a.bs = 1;
+  a.k_store_w = store_width(y, rb, 0, 0, rb);
+  a.vec_ok_k = vec_aligned(x, x_dtype, D, 0);
+  return launch_store(a, stream);
+}
+
+extern "C" cudaError_t launch_reshape_and_cache_q8(
+    const void* key, const int64_t* slot_mapping, uint8_t* k_cache_q8, int num_tokens,
+    int num_kv_heads, int head_size, int block_size, int64_t key_token_stride,
+    int64_t key_head_stride, int64_t cache_block_stride, int64_t cache_token_stride,
+    int64_t cache_head_stride, cudaStream_t stream) {
+  return gfx906_fa_store_kv(key, G9_DT_F16, key_token_stride, key_head_stride, nullptr, G9_DT_F16, 0, 0,
+                            slot_mapping, k_cache_q8, cache_block_stride, cache_token_stride,
+                            cache_head_stride, nullptr, 0, 0, 0, G9_V_NONE, num_tokens, num_kv_heads,
+                            head_size, block_size, stream);
+}
+
+extern "C" cudaError_t gfx906_fa_store_kv(
+    const void* key, int key_dtype, int64_t key_token_stride, int64_t key_head_stride,
+    const void* value, int value_dtype, int64_t value_token_stride, int64_t value_head_stride,
+    const int64_t* slot_mapping, uint8_t* k_cache, int64_t k_block_stride, int64_t k_token_stride,
+    int64_t k_head_stride, uint8_t* v_cache, int64_t v_block_stride, int64_t v_token_stride,
+    int64_t v_head_stride, int v_mode, int num_tokens, int num_kv_heads, int head_size,
+    int block_size, cudaStream_t stream) {
+  if (head_size % QK != 0 || head_size <= 0 || head_size > kMaxD) return cudaErrorInvalidValue;
+  if (num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0) return cudaErrorInvalidValue;
+  if (key_dtype < 0 || key_dtype > 2) return cudaErrorInvalidValue;
+  if (v_mode < 0 || v_mode > 2) return cudaErrorInvalidValue;
+  if (v_mode == G9_V_COPY16 && value_dtype == G9_DT_F32) return cudaErrorInvalidValue;
+  if (v_mode != G9_V_NONE && (value == nullptr || v_cache == nullptr)) return cudaErrorInvalidValue;
+  if (num_tokens == 0) return cudaSuccess;
+  StoreArgs a{};
+  const int rb = q8_row_bytes(head_size);
+  a.key = key; a.key_dt = key_dtype; a.key_tok = key_token_stride; a.key_head = key_head_stride;
+  a.value = value; a.val_dt = value_dtype; a.val_tok = value_token_stride; a.val_head = value_head_stride;
+  a.slot_mapping = slot_mapping;
+  a.k_cache = k_cache; a.kc_blk = k_block_stride; a.kc_tok = k_token_stride; a.kc_head = k_head_stride;
+  a.v_cache = v_cache; a.vc_blk = v_block_stride; a.vc_tok = v_token_stride; a.vc_head = v_head_stride;
+  a.v_mode = v_mode;
+  a.T = num_tokens; a.Hkv = num_kv_heads; a.D = head_size; a.bs = block_size;
+  a.k_store_w = store_width(k_cache, k_block_stride, k_token_stride, k_head_stride, rb);
+  a.vec_ok_k = vec_aligned(key, key_dtype, key_token_stride, key_head_stride);
+  if (v_mode == G9_V_Q8) {
+    a.v_store_w = store_width(v_cache, v_block_stride, v_token_stride, v_head_stride, rb);
+    a.vec_ok_v = vec_aligned(value, value_dtype, value_token_stride, value_head_stride);
+  } else if (v_mode == G9_V_COPY16) {
+    a.v_store_w = store_width(v_cache, v_block_stride, v_token_stride, v_head_stride, 2 * head_size);
+    a.vec_ok_v = vec_aligned(value, value_dtype, value_token_stride, value_head_stride);
+  }
+  return launch_store(a, stream);
+}

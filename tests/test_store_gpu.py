@@ -1,0 +1,172 @@
+"""Q8_0 store / quant kernels on the GPU, bit-exact against the CPU oracle.
+
+Mirrors the reference's tests/test_quant.py (dense quant, store by slot,
+slot -1 skipped, untouched slots stay zero) with the tolerance tightened from
+"<= 1 LSB, < 1 % bytes" to bit-exact: the oracle restates the device kernel's
+fp32 arithmetic, not the reference's double-precision CPU helper.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from _util import to_np
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _gfx():
+    import gfx906_fa
+    return gfx906_fa
+
+
+def _rand(shape, dtype, seed, scale=1.0, outliers=0.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(shape, generator=g) * scale
+    if outliers:
+        m = torch.rand(shape, generator=g) < outliers
+        x = torch.where(m, x * 8, x)
+    return x.to(dtype)
+
+
+def _oracle_quant(x):
+    if x.dtype == torch.bfloat16:
+        return O.quantize_q8_0(to_np(x), "bf16")
+    return O.quantize_q8_0(to_np(x))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("shape", [(1, 32), (4, 128), (2, 8, 128), (1, 4, 64, 128), (3, 5, 64), (7, 256)])
+def test_quantize_dense_bitexact(dtype, shape):
+    x = _rand(shape, dtype, seed=hash(shape) % 1000, scale=0.5, outliers=0.01)
+    y = _gfx().quantize_q8_0(x.to(dev))
+    assert y.dtype == torch.uint8 and tuple(y.shape) == shape[:-1] + (shape[-1] // 32 * 34,)
+    assert np.array_equal(to_np(y), _oracle_quant(x))
+
+
+def test_quantize_dense_edge_values():
+    x = torch.zeros((6, 128), dtype=torch.float16)
+    x[1, 5] = 1.0
+    x[2, :32] = torch.arange(32, dtype=torch.float16) - 16
+    x[3] = 65504.0
+    x[4] = (torch.randn(128) * 1e-6).half()          # fp16 subnormals
+    x[5, ::2] = -3.0
+    y = _gfx().quantize_q8_0(x.to(dev))
+    assert np.array_equal(to_np(y), _oracle_quant(x))
+
+
+def test_quantize_dense_large_config2_shape():
+    """16 x 4096 tokens x 8 heads x 128, 1 % outliers x8."""
+    x = _rand((16 * 4096, 8, 128), torch.float16, seed=7, outliers=0.01)
+    y = _gfx().quantize_q8_0(x.to(dev))
+    assert np.array_equal(to_np(y), _oracle_quant(x))
+
+
+def test_reshape_and_cache_q8_slots():
+    NB, bs, Hkv, D = 10, 16, 4, 128
+    rb = D // 32 * 34
+    slots = torch.tensor([5, 10, 20, 21, 22], dtype=torch.int64)
+    key = _rand((5, Hkv, D), torch.float16, seed=3, scale=0.3)
+    cache = torch.zeros((NB, bs, Hkv, rb), dtype=torch.uint8, device=dev)
+    _gfx().reshape_and_cache_q8(key.to(dev), slots.to(dev), cache)
+    ref = np.zeros((NB, bs, Hkv, rb), np.uint8)
+    O.reshape_and_cache(to_np(key), slots.numpy(), ref)
+    assert np.array_equal(to_np(cache), ref)
+
+
+def test_reshape_and_cache_q8_skip_negative_slot():
+    NB, bs, Hkv, D = 4, 16, 2, 64
+    rb = D // 32 * 34
+    slots = torch.tensor([0, -1, 5], dtype=torch.int64)
+    key = _rand((3, Hkv, D), torch.float16, seed=4)
+    cache = torch.zeros((NB, bs, Hkv, rb), dtype=torch.uint8, device=dev)
+    _gfx().reshape_and_cache_q8(key.to(dev), slots.to(dev), cache)
+    c = to_np(cache)
+    q = _oracle_quant(key)
+    assert np.array_equal(c[0, 0], q[0]) and np.array_equal(c[0, 5], q[2])
+    mask = np.ones((NB, bs), bool)
+    mask[0, 0] = mask[0, 5] = False
+    assert (c[mask] == 0).all()
+
+
+def test_reshape_and_cache_q8_strided_key():
+    """key as a slice of a fused qkv tensor (token stride > Hkv * D)."""
+    T, Hq, Hkv, D, NB, bs = 37, 6, 2, 128, 8, 16
+    qkv = _rand((T, Hq + 2 * Hkv, D), torch.float16, seed=5)
+    key = qkv.to(dev)[:, Hq:Hq + Hkv]
+    slots = torch.randperm(NB * bs, generator=torch.Generator().manual_seed(1))[:T].to(torch.int64)
+    cache = torch.zeros((NB, bs, Hkv, D // 32 * 34), dtype=torch.uint8, device=dev)
+    _gfx().reshape_and_cache_q8(key, slots.to(dev), cache)
+    ref = np.zeros(tuple(cache.shape), np.uint8)
+    O.reshape_and_cache(to_np(qkv[:, Hq:Hq + Hkv]), slots.numpy(), ref)
+    assert np.array_equal(to_np(cache), ref)
+
+
+@pytest.mark.parametrize("vdtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("v_mode", [1, 2])
+def test_store_kv_fused(vdtype, v_mode):
+    """Fused K (Q8_0) + V (copy or Q8_0) store into one vLLM-shaped
+    [NB, 2, bs, Hkv, D] cache viewed as bytes, slots with -1 padding."""
+    T, Hkv, D, NB, bs = 50, 8, 128, 12, 16
+    key = _rand((T, Hkv, D), vdtype, seed=10)
+    val = _rand((T, Hkv, D), vdtype, seed=11, outliers=0.01)
+    slots = torch.randperm(NB * bs, generator=torch.Generator().manual_seed(2))[:T].to(torch.int64)
+    slots[3] = -1
+    kv = torch.zeros((NB, 2, bs, Hkv, D), dtype=vdtype, device=dev)
+    kb = kv.view(torch.uint8)                                   # [NB, 2, bs, Hkv, 2D] bytes
+    rb = D // 32 * 34
+    k_view = kb[:, 0, :, :, :rb]
+    v_view = kb[:, 1, :, :, :rb] if v_mode == 2 else kv[:, 1]
+    _gfx().store_kv(key.to(dev), val.to(dev), slots.to(dev), k_view, v_view, v_mode)
+    got = to_np(kb)
+    # oracle
+    ref_k = np.zeros((NB, bs, Hkv, rb), np.uint8)
+    tag = "bf16" if vdtype == torch.bfloat16 else None
+    O.reshape_and_cache(to_np(key), slots.numpy(), ref_k, tag)
+    assert np.array_equal(got[:, 0, :, :, :rb], ref_k)
+    assert (got[:, 0, :, :, rb:] == 0).all()
+    if v_mode == 2:
+        ref_v = np.zeros((NB, bs, Hkv, rb), np.uint8)
+        O.reshape_and_cache(to_np(val), slots.numpy(), ref_v, tag)
+        assert np.array_equal(got[:, 1, :, :, :rb], ref_v)
+    else:
+        ref_v = np.zeros((NB, bs, Hkv, D), np.uint16)
+        O.store_v16(to_np(val).view(np.uint16), slots.numpy(), ref_v)
+        assert np.array_equal(got[:, 1].view(np.uint16), ref_v)
+
+
+def test_store_kv_through_c_abi():
+    """Same store, called directly through the C ABI with raw pointers."""
+    import ctypes
+    from _util import capi
+    lib = capi()
+    T, Hkv, D, NB, bs = 20, 2, 128, 4, 16
+    rb = D // 32 * 34
+    key = _rand((T, Hkv, D), torch.float16, seed=12).to(dev)
+    slots = torch.arange(T, dtype=torch.int64, device=dev) * 3
+    cache = torch.zeros((NB, bs, Hkv, rb), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    i64 = ctypes.c_int64
+    rc = lib.gfx906_fa_store_kv(
+        ctypes.c_void_p(key.data_ptr()), 0, i64(Hkv * D), i64(D), None, 0, i64(0), i64(0),
+        ctypes.c_void_p(slots.data_ptr()), ctypes.c_void_p(cache.data_ptr()), i64(bs * Hkv * rb),
+        i64(Hkv * rb), i64(rb), None, i64(0), i64(0), i64(0), 0, T, Hkv, D, bs, ctypes.c_void_p(stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = np.zeros((NB, bs, Hkv, rb), np.uint8)
+    O.reshape_and_cache(to_np(key), to_np(slots), ref)
+    assert np.array_equal(to_np(cache), ref)
+    assert _gfx().device_error(True) == 0
+
+
+def test_rejects_bad_inputs():
+    g = _gfx()
+    with pytest.raises(RuntimeError):
+        g.quantize_q8_0(torch.zeros((4, 48), dtype=torch.float16, device=dev))
+    with pytest.raises(RuntimeError):
+        g.quantize_q8_0(torch.zeros((4, 128), dtype=torch.float16))          # CPU tensor
+    with pytest.raises(RuntimeError):
+        g.reshape_and_cache_q8(torch.zeros((2, 2, 128), dtype=torch.float16, device=dev),
+                               torch.zeros(2, dtype=torch.int32, device=dev),
+                               torch.zeros((2, 16, 2, 136), dtype=torch.uint8, device=dev))
