@@ -1,0 +1,760 @@
+// attn_decode.cu -- split-K flash decoding straight from the paged Q8_0 cache.
+//
+// Replaces the reference's direct-paged tile kernel
+// (kernel/fattn-q8-paged.cuh:381-641, launched by gfx906_fa_launch_paged,
+// extension/gfx906_fa_launcher.cu:222-352) for short query chunks.  Design:
+//
+//  * Persistent CTAs (one per SM): warpgroups 0-1 compute (8 warps),
+//    warpgroup 2 produces (warp 8 issues copies, warps 9-11 only hand their
+//    registers to the compute warps through setmaxnreg).  The work list is
+//    (KV chunk, kv-head group, sequence); CTAs walk it round-robin and the
+//    producer keeps prefetching across item boundaries, so HBM stays busy
+//    while a chunk's epilogue runs.
+//  * The producer streams whole pages with bulk-async copies (TMA engine)
+//    into a 3-slot shared-memory ring, one mbarrier per slot for "full" and
+//    one for "empty".  Rows of one token (all heads of the group) are copied
+//    contiguously and padded to an odd multiple of 16 bytes, which makes the
+//    tensor-core operand loads bank-conflict free.
+//  * GQA packing: one warp owns one kv head and computes all G query heads x
+//    n_q query tokens of it (rows r = t*G + g, up to 32) against each page:
+//    S = Q.K^T with mma.sync m16n8k16 (Q in fp16, K int8 converted exactly to
+//    fp16, the per-block fp16 scale applied in fp32 after each 32-wide block),
+//    online softmax in base 2, O += P.V with P in fp16 (bf16 for bf16 V) and
+//    V as stored (or Q8_0 dequantised to fp16 in registers).  So the only
+//    roundings beyond fp32 are Q and P to 16 bits and, for Q8_0 V, the
+//    dequantised V to fp16.
+//  * With fewer than 8 kv heads per CTA, the warps of one head split the
+//    pages of a stage and merge their softmax states at the end of a chunk.
+//  * A chunk's result is final when the sequence has one chunk; otherwise
+//    the normalised partial O and its (max, sum) go to the workspace and a
+//    combine kernel merges them (log-sum-exp weights).
+//
+// Masking follows the reference: keys at k >= kv_len are ignored, with
+// q_abs the causal rule is k <= q_abs[b] + t (fattn-q8.cuh:646-654), and an
+// optional fp16 additive mask is added to the scaled score.  Rows without any
+// visible key produce zeros.  Every mbarrier wait is bounded (common.cuh).
+#include <algorithm>
+
+#include "attn_common.cuh"
+
+namespace g9 {
+
+namespace dec {
+constexpr int D = 128;
+constexpr int PAGE = 16;
+constexpr int NWC = 8;                      // compute warps (warpgroups 0, 1)
+constexpr int NTHREADS = 384;               // + warpgroup 2: warp 8 produces, 9-11 exit
+constexpr int NST = 3;                      // pipeline slots
+constexpr int MAXP = 8;                     // max pages per stage
+constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
+// setmaxnreg split: launch 384 threads x 168 = 64512 = 256*232 + 128*40
+constexpr int REG_COMPUTE = 232;
+constexpr int REG_PRODUCER = 40;
+}  // namespace dec
+
+struct DecodeParams {
+  G9AttnBatch p;
+  int G;                  // query heads per kv head
+  int HG;                 // kv heads per CTA
+  int HGN;                // head groups (num_heads_kv / HG)
+  int P;                  // pages per stage (= warps per head)
+  int CP;                 // pages per chunk (multiple of P)
+  int S_max;              // chunks per sequence (upper bound)
+  int n_items;
+  int R_pad;              // 16 * MT
+  int rb_k, rb_v;         // bytes of one K / V row
+  int kstride, vstride;   // smem bytes per token row group
+  int k_whole, v_whole;   // 1: one copy per page (else one per token)
+  int kpage, vpage;       // smem bytes per page
+  int stage_bytes;
+  int merge_off;          // smem offset of the merge buffer
+  int q_off;              // smem offset of the Q tiles (MT == 2)
+  int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
+  float scale_log2;
+  float* opart;           // [B][Hkv][S_max][R_pad][D]
+  float2* ml;             // [B][Hkv][S_max][R_pad]
+};
+
+struct StageMeta {
+  int item, page0, npages, last;
+  int ok[dec::MAXP];
+};
+
+__device__ __forceinline__ void decode_item(const DecodeParams& d, int item, int& b, int& z, int& s) {
+  const int per = d.p.num_seqs * d.HGN;
+  s = item / per;
+  const int rem = item - s * per;
+  b = rem / d.HGN;
+  z = rem - b * d.HGN;
+}
+
+// page range [pb, pe) of an item; returns false for items with nothing to do.
+// An item with pe == pb (sequence without visible keys) is still emitted for
+// chunk 0 so that zeros get written.
+__device__ __forceinline__ bool item_pages(const DecodeParams& d, int b, int s, int& pb, int& pe,
+                                           int& nsplit) {
+  const int nq = seq_nq(d.p, b);
+  const int kv_end = seq_kv_end(d.p, b, nq);
+  const int npg = (kv_end + dec::PAGE - 1) / dec::PAGE;
+  nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;
+  if (nq <= 0 || nq * d.G > d.max_rows || s >= nsplit) return false;
+  pb = s * d.CP;
+  pe = min(npg, pb + d.CP);
+  return true;
+}
+
+__device__ __forceinline__ void named_sync_compute() {
+  asm volatile("bar.sync 1, %0;" ::"n"(dec::NWC * 32) : "memory");
+}
+
+// MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0).
+template <int MT, int VT, bool MASK>
+__global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodeParams d) {
+  using namespace dec;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full_bar[NST];
+  __shared__ __align__(8) uint64_t empty_bar[NST];
+  __shared__ StageMeta meta[NST];
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const G9AttnBatch& p = d.p;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NST; ++i) {
+      mbar_init(&full_bar[i], 1);
+      mbar_init(&empty_bar[i], NWC);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // =========================================================================
+  // producer warpgroup (warp 8 issues copies, 9-11 only give up registers)
+  // =========================================================================
+  if (warp >= NWC) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
+    if (warp != NWC) return;
+    int it = 0;
+    bool alive = true;
+    const int hgb_k = d.HG * d.rb_k, hgb_v = d.HG * d.rb_v;
+    const int ncopy_k = d.k_whole ? 1 : PAGE;
+    const int ncopy_v = d.v_whole ? 1 : PAGE;
+    const uint32_t kbytes_page = (uint32_t)(PAGE * hgb_k);
+    const uint32_t vbytes_page = (uint32_t)(PAGE * hgb_v);
+    const int per_page = ncopy_k + ncopy_v;
+    for (int item = blockIdx.x; item < d.n_items && alive; item += gridDim.x) {
+      int b, z, s, pb, pe, nsplit;
+      decode_item(d, item, b, z, s);
+      if (!item_pages(d, b, s, pb, pe, nsplit)) continue;
+      const int h0 = z * d.HG;
+      for (int pg = pb;; pg += d.P) {
+        const int slot = it % NST;
+        if (it >= NST && !mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) { alive = false; break; }
+        const int npg = max(0, min(d.P, pe - pg));
+        int phys = -1;
+        if (lane < npg) phys = p.block_table[(int64_t)b * p.max_blocks + pg + lane];
+        const bool ok = lane < npg && phys >= 0;
+        if (lane < npg && phys < 0) raise_error(ERR_BAD_PAGE);
+        if (lane < MAXP) meta[slot].ok[lane] = ok ? 1 : 0;
+        const unsigned okmask = __ballot_sync(0xffffffffu, ok);
+        const bool last = pg + d.P >= pe;
+        if (lane == 0) {
+          meta[slot].item = item;
+          meta[slot].page0 = pg;
+          meta[slot].npages = npg;
+          meta[slot].last = last ? 1 : 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], __popc(okmask) * (kbytes_page + vbytes_page));
+        __syncwarp();
+        uint8_t* kdst0 = smem + slot * d.stage_bytes;
+        uint8_t* vdst0 = kdst0 + d.P * d.kpage;
+        // uniform trip count for the whole warp (the shuffle needs every lane)
+        for (int c0 = 0; c0 < d.P * per_page; c0 += 32) {
+          const int c = c0 + lane;
+          const int j = min(c / per_page, MAXP - 1);
+          const int r = c - j * per_page;
+          const int phys_j = __shfl_sync(0xffffffffu, phys, j);
+          if (c >= d.P * per_page || j >= npg || !((okmask >> j) & 1)) continue;
+          if (r < ncopy_k) {
+            const uint8_t* src = p.k_cache + (int64_t)phys_j * p.k_page_stride + (int64_t)h0 * p.k_head_stride;
+            if (d.k_whole) {
+              bulk_g2s(kdst0 + j * d.kpage, src, PAGE * hgb_k, &full_bar[slot]);
+            } else {
+              bulk_g2s(kdst0 + j * d.kpage + r * d.kstride, src + (int64_t)r * p.k_tok_stride, hgb_k,
+                       &full_bar[slot]);
+            }
+          } else {
+            const int t = r - ncopy_k;
+            const uint8_t* src = p.v_cache + (int64_t)phys_j * p.v_page_stride + (int64_t)h0 * p.v_head_stride;
+            if (d.v_whole) {
+              bulk_g2s(vdst0 + j * d.vpage, src, PAGE * hgb_v, &full_bar[slot]);
+            } else {
+              bulk_g2s(vdst0 + j * d.vpage + t * d.vstride, src + (int64_t)t * p.v_tok_stride, hgb_v,
+                       &full_bar[slot]);
+            }
+          }
+        }
+        ++it;
+        if (last) break;
+      }
+    }
+    // terminator stage
+    if (alive) {
+      const int slot = it % NST;
+      if (it < NST || mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) {
+        if (lane == 0) {
+          meta[slot].item = -1;
+          mbar_arrive(&full_bar[slot]);
+        }
+      }
+    }
+    return;
+  }
+
+  // =========================================================================
+  // compute warps
+  // =========================================================================
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
+  const int hl = warp % d.HG;       // local kv head
+  const int sub = warp / d.HG;      // page slot within a stage
+  const int j4 = lane & 3;          // quad lane
+  const int rq = lane >> 2;         // row within an 8-row group
+
+  constexpr bool QS = MT == 2;      // Q tile in shared memory instead of registers
+  uint32_t qa[QS ? 1 : MT][8][4];   // Q fragments (fp16), MT == 1 only
+  float o[MT][16][4];
+  float mrow[MT][2], lrow[MT][2];
+  int cur_item = -1, cb = 0, cz = 0, cs = 0, cnq = 0, cR = 0, ckv = 0, cqabs = 0, cnsplit = 1;
+
+  auto reset_state = [&]() {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) o[mt][nt][c] = 0.f;
+      mrow[mt][0] = mrow[mt][1] = -INFINITY;
+      lrow[mt][0] = lrow[mt][1] = 0.f;
+    }
+  };
+
+  const uint32_t smem_base = smem_u32(smem);
+  const uint32_t qs_base = smem_base + d.q_off + hl * (MT * 16 * QROW);
+
+  auto load_q = [&](int b, int h) {
+    if constexpr (QS) {
+      // warps sharing a head write the same tile; sync before and after so no
+      // warp still reads the previous item's tile
+      named_sync_compute();
+      if (sub == 0) {
+        for (int i = lane; i < MT * 16 * 64; i += 32) {   // 64 element pairs per row
+          const int r = i >> 6, c = (i & 63) * 2;
+          float x0 = 0.f, x1 = 0.f;
+          if (r < cR) {
+            const int t = r / d.G;
+            const int64_t base = q_offset(p, b, t, h * d.G + (r - t * d.G));
+            x0 = load_one(p.q, base + c, p.q_dtype);
+            x1 = load_one(p.q, base + c + 1, p.q_dtype);
+          }
+          const uint32_t v = pack_half2(x0, x1);
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(qs_base + r * QROW + c * 2), "r"(v));
+        }
+      }
+      named_sync_compute();
+    } else {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = rq + half * 8;
+        const bool valid = r < cR;
+        const int t = valid ? r / d.G : 0;
+        const int hq = h * d.G + (valid ? r - t * d.G : 0);
+        const int64_t base = valid ? q_offset(p, b, t, hq) : 0;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+          for (int hi = 0; hi < 2; ++hi) {
+            const int dd = ks * 16 + hi * 8 + 2 * j4;
+            float x0 = 0.f, x1 = 0.f;
+            if (valid) {
+              x0 = load_one(p.q, base + dd, p.q_dtype);
+              x1 = load_one(p.q, base + dd + 1, p.q_dtype);
+            }
+            // a0: (row, k lo)  a1: (row+8, k lo)  a2: (row, k hi)  a3: (row+8, k hi)
+            qa[0][ks][hi * 2 + half] = pack_half2(x0, x1);
+          }
+        }
+      }
+    }
+  };
+
+  // A fragment of Q for (m-tile mt, k-step ks)
+  auto q_frag = [&](int mt, int ks, uint32_t a[4]) {
+    if constexpr (QS) {
+      // matrices: (rows 0-7 | 8-15) x (k 0-7 | 8-15) -> a0..a3
+      const int mi = lane >> 3, ri = lane & 7;
+      const uint32_t addr = qs_base + (mt * 16 + (mi & 1) * 8 + ri) * QROW + ks * 32 + (mi >> 1) * 16;
+      asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                   : "r"(addr));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = qa[0][ks][i];
+    }
+  };
+
+  float* merge = reinterpret_cast<float*>(smem + d.merge_off);
+
+  auto epilogue = [&]() {
+    // quad-reduce the running sums
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float v = lrow[mt][hh];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        lrow[mt][hh] = v;
+      }
+    // merge the warps that share a kv head (fragment order: lane-contiguous)
+    const int wph = NWC / d.HG;
+    float* mb = merge + (size_t)hl * (MT * (16 * 4 + 4) * 32);
+    for (int rr = 1; rr < wph; ++rr) {
+      if (sub == rr) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) mb[((mt * 16 + nt) * 4 + c) * 32 + lane] = o[mt][nt][c];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            mb[(MT * 64 + mt * 4 + hh) * 32 + lane] = mrow[mt][hh];
+            mb[(MT * 64 + mt * 4 + 2 + hh) * 32 + lane] = lrow[mt][hh];
+          }
+        }
+      }
+      named_sync_compute();
+      if (sub == 0) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          float a0[2], a1[2];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float m1 = mb[(MT * 64 + mt * 4 + hh) * 32 + lane];
+            const float l1 = mb[(MT * 64 + mt * 4 + 2 + hh) * 32 + lane];
+            const float mn = fmaxf(mrow[mt][hh], m1);
+            const float mu = mn == -INFINITY ? 0.f : mn;
+            a0[hh] = fast_exp2(mrow[mt][hh] - mu);
+            a1[hh] = fast_exp2(m1 - mu);
+            mrow[mt][hh] = mn;
+            lrow[mt][hh] = lrow[mt][hh] * a0[hh] + l1 * a1[hh];
+          }
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              o[mt][nt][c] = o[mt][nt][c] * a0[c >> 1] + mb[((mt * 16 + nt) * 4 + c) * 32 + lane] * a1[c >> 1];
+        }
+      }
+      named_sync_compute();
+    }
+    if (sub != 0) return;
+    const int h = cz * d.HG + hl;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int r = mt * 16 + rq + hh * 8;
+        if (r >= cR) continue;
+        const float l = lrow[mt][hh];
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        if (cnsplit == 1) {
+          const int t = r / d.G;
+          const int hq = h * d.G + (r - t * d.G);
+          const int64_t ob = o_offset(p, cb, t, hq);
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt)
+            store_out2(p.out, p.out_dtype, ob + nt * 8 + 2 * j4, o[mt][nt][hh * 2] * inv,
+                       o[mt][nt][hh * 2 + 1] * inv);
+        } else {
+          const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_max + cs) * d.R_pad + r;
+          float* op = d.opart + row * D;
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt)
+            *reinterpret_cast<float2*>(op + nt * 8 + 2 * j4) =
+                make_float2(o[mt][nt][hh * 2] * inv, o[mt][nt][hh * 2 + 1] * inv);
+          if (j4 == 0) d.ml[row] = make_float2(mrow[mt][hh], l);
+        }
+      }
+    }
+  };
+
+  for (int it = 0;; ++it) {
+    const int slot = it % NST;
+    if (!mbar_wait(&full_bar[slot], (it / NST) & 1)) break;
+    const int item = meta[slot].item;
+    if (item < 0) break;
+    const int page0 = meta[slot].page0;
+    const int npages = meta[slot].npages;
+    const bool last = meta[slot].last != 0;
+    const bool page_ok = sub < npages && meta[slot].ok[sub];
+    if (item != cur_item) {
+      cur_item = item;
+      decode_item(d, item, cb, cz, cs);
+      cnq = seq_nq(p, cb);
+      cR = cnq * d.G;
+      ckv = p.kv_len[cb];
+      cqabs = p.q_abs ? p.q_abs[cb] : 0;
+      int pb, pe;
+      item_pages(d, cb, cs, pb, pe, cnsplit);
+      reset_state();
+      load_q(cb, cz * d.HG + hl);
+    }
+    if (page_ok) {
+      const int pg = page0 + sub;
+      const int k0 = pg * PAGE;
+      const uint32_t kb = smem_base + slot * d.stage_bytes + sub * d.kpage + hl * d.rb_k;
+      const uint32_t vb = smem_base + slot * d.stage_bytes + d.P * d.kpage + sub * d.vpage + hl * d.rb_v;
+      // ---------------- S = Q K^T --------------------------------------------
+      float sacc[MT][2][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) sacc[mt][nt][c] = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint32_t krow = kb + (nt * 8 + rq) * d.kstride;            // B operand row (key)
+        const uint32_t kcol0 = kb + (nt * 8 + 2 * j4) * d.kstride;       // accumulator column keys
+        const uint32_t kcol1 = kcol0 + d.kstride;
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          const uint32_t qb = krow + blk * QBLOCK + 2 + 2 * j4;
+          uint32_t b0[2], b1[2];
+          b0[0] = i8x2_to_h2(lds_u16(qb));
+          b0[1] = i8x2_to_h2(lds_u16(qb + 8));
+          b1[0] = i8x2_to_h2(lds_u16(qb + 16));
+          b1[1] = i8x2_to_h2(lds_u16(qb + 24));
+          const float dk0 = half_bits_to_float(lds_u16(kcol0 + blk * QBLOCK));
+          const float dk1 = half_bits_to_float(lds_u16(kcol1 + blk * QBLOCK));
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t a0[4], a1[4];
+            q_frag(mt, 2 * blk, a0);
+            q_frag(mt, 2 * blk + 1, a1);
+            mma_f16_16816(acc, a0, b0);
+            mma_f16_16816(acc, a1, b1);
+            sacc[mt][nt][0] = fmaf(acc[0], dk0, sacc[mt][nt][0]);
+            sacc[mt][nt][1] = fmaf(acc[1], dk1, sacc[mt][nt][1]);
+            sacc[mt][nt][2] = fmaf(acc[2], dk0, sacc[mt][nt][2]);
+            sacc[mt][nt][3] = fmaf(acc[3], dk1, sacc[mt][nt][3]);
+          }
+        }
+      }
+      // ---------------- mask + online softmax (base 2) ------------------------
+      uint32_t pa[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int r = mt * 16 + rq + hh * 8;
+          const int t = r / d.G;
+          int kv_lim = ckv;                                      // exclusive
+          if (p.q_abs) kv_lim = min(kv_lim, cqabs + t + 1);
+          if (r >= cR) kv_lim = -1;
+          float mx = -INFINITY;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int k = k0 + nt * 8 + 2 * j4 + c;
+              float x = sacc[mt][nt][hh * 2 + c] * d.scale_log2;
+              if constexpr (MASK) {
+                if (r < cR && k < ckv)
+                  x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                      (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+              }
+              x = k < kv_lim ? x : -INFINITY;
+              sacc[mt][nt][hh * 2 + c] = x;
+              mx = fmaxf(mx, x);
+            }
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float mn = fmaxf(mrow[mt][hh], mx);
+          const float mu = mn == -INFINITY ? 0.f : mn;
+          const float alpha = fast_exp2(mrow[mt][hh] - mu);
+          mrow[mt][hh] = mn;
+          float ls = 0.f;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const float pv = fast_exp2(sacc[mt][nt][hh * 2 + c] - mu);
+              sacc[mt][nt][hh * 2 + c] = pv;
+              ls += pv;
+            }
+          lrow[mt][hh] = lrow[mt][hh] * alpha + ls;
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt) {
+            o[mt][nt][hh * 2] *= alpha;
+            o[mt][nt][hh * 2 + 1] *= alpha;
+          }
+        }
+        if constexpr (VT == 1) {
+          pa[mt][0] = pack_bf162(sacc[mt][0][0], sacc[mt][0][1]);
+          pa[mt][1] = pack_bf162(sacc[mt][0][2], sacc[mt][0][3]);
+          pa[mt][2] = pack_bf162(sacc[mt][1][0], sacc[mt][1][1]);
+          pa[mt][3] = pack_bf162(sacc[mt][1][2], sacc[mt][1][3]);
+        } else {
+          pa[mt][0] = pack_half2(sacc[mt][0][0], sacc[mt][0][1]);
+          pa[mt][1] = pack_half2(sacc[mt][0][2], sacc[mt][0][3]);
+          pa[mt][2] = pack_half2(sacc[mt][1][0], sacc[mt][1][1]);
+          pa[mt][3] = pack_half2(sacc[mt][1][2], sacc[mt][1][3]);
+        }
+      }
+      // ---------------- O += P V ------------------------------------------------
+      if constexpr (VT != 2) {
+        // ldmatrix.trans: thread i addresses matrix i/8 row i%8; matrices
+        // (keys 0-7 | 8-15) x (d block nt | nt+1)
+        const int mi = lane >> 3, ri = lane & 7;
+        const uint32_t vrow = vb + ((mi & 1) * 8 + ri) * d.vstride + (mi >> 1) * 16;
+#pragma unroll
+        for (int ntp = 0; ntp < 8; ++ntp) {
+          uint32_t r4[4];
+          ldmatrix_x4_trans(r4, vrow + ntp * 32);
+          const uint32_t bA[2] = {r4[0], r4[1]};
+          const uint32_t bB[2] = {r4[2], r4[3]};
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            if constexpr (VT == 1) {
+              mma_bf16_16816(o[mt][2 * ntp], pa[mt], bA);
+              mma_bf16_16816(o[mt][2 * ntp + 1], pa[mt], bB);
+            } else {
+              mma_f16_16816(o[mt][2 * ntp], pa[mt], bA);
+              mma_f16_16816(o[mt][2 * ntp + 1], pa[mt], bB);
+            }
+          }
+        }
+      } else {
+        // V rows are Q8_0: B fragment element (key k, dim n) = q8[k][n] * d[k][n/32]
+        const uint32_t r0 = vb + (2 * j4) * d.vstride;       // keys 2j, 2j+1, 2j+8, 2j+9
+        const uint32_t r1 = r0 + d.vstride;
+        const uint32_t r8 = r0 + 8 * d.vstride;
+        const uint32_t r9 = r8 + d.vstride;
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          const uint32_t so = blk * QBLOCK;
+          const __half2 s01 = __halves2half2(__ushort_as_half(lds_u16(r0 + so)), __ushort_as_half(lds_u16(r1 + so)));
+          const __half2 s89 = __halves2half2(__ushort_as_half(lds_u16(r8 + so)), __ushort_as_half(lds_u16(r9 + so)));
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int nt = blk * 4 + q;
+            const uint32_t off = so + 2 + q * 8 + rq;          // dim n = nt*8 + rq
+            uint32_t v0, v1, v8, v9;
+            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v0) : "r"(r0 + off));
+            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v1) : "r"(r1 + off));
+            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v8) : "r"(r8 + off));
+            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v9) : "r"(r9 + off));
+            uint32_t h01 = i8x2_to_h2(v0 | (v1 << 8));
+            uint32_t h89 = i8x2_to_h2(v8 | (v9 << 8));
+            __half2 x01 = __hmul2(*reinterpret_cast<__half2*>(&h01), s01);
+            __half2 x89 = __hmul2(*reinterpret_cast<__half2*>(&h89), s89);
+            const uint32_t bq[2] = {*reinterpret_cast<uint32_t*>(&x01), *reinterpret_cast<uint32_t*>(&x89)};
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][nt], pa[mt], bq);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    if (last) epilogue();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// combine: merge the per-chunk partial results of sequences with >1 chunk
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams d) {
+  const G9AttnBatch& p = d.p;
+  const int b = blockIdx.y;
+  const int h = blockIdx.x;
+  const int nq = seq_nq(p, b);
+  if (nq <= 0 || nq * d.G > d.max_rows) return;
+  const int kv_end = seq_kv_end(p, b, nq);
+  const int npg = (kv_end + dec::PAGE - 1) / dec::PAGE;
+  const int nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;
+  if (nsplit <= 1) return;
+  const int R = nq * d.G;
+  const int dd = threadIdx.x;
+  for (int r = 0; r < R; ++r) {
+    const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_max) * d.R_pad + r;
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
+    const float mu = M == -INFINITY ? 0.f : M;
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float2 ml = d.ml[row0 + (int64_t)s * d.R_pad];
+      const float w = ml.y * fast_exp2(ml.x - mu);
+      den += w;
+      num += w * d.opart[(row0 + (int64_t)s * d.R_pad) * dec::D + dd];
+    }
+    const float v = den > 0.f ? num / den : 0.f;
+    const int t = r / d.G;
+    const int hq = h * d.G + (r - t * d.G);
+    const int64_t off = o_offset(p, b, t, hq) + dd;
+    if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = v;
+    else if (p.out_dtype == DT_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static int pad_odd16(int bytes) {
+  int s = (bytes + 15) & ~15;
+  if (((s / 16) & 1) == 0) s += 16;
+  return s;
+}
+
+static int num_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// Fills DecodeParams from the batch; returns cudaErrorInvalidValue when the
+// batch is outside what the decode kernel handles.
+static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
+  using namespace dec;
+  if (p.head_dim != D || p.block_size != PAGE) return cudaErrorInvalidValue;
+  if (p.num_seqs < 0 || p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv)
+    return cudaErrorInvalidValue;
+  if (p.seq_q < 0 || p.max_kv < 0 || p.max_blocks < 0) return cudaErrorInvalidValue;
+  if (p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2 || p.v_fmt < 0 || p.v_fmt > 2)
+    return cudaErrorInvalidValue;
+  d = DecodeParams{};
+  d.p = p;
+  d.G = p.num_heads_q / p.num_heads_kv;
+  const int R = std::min(d.G * std::max(p.seq_q, 1), 32);
+  mt = R <= 16 ? 1 : 2;
+  d.max_rows = R;
+  d.R_pad = 16 * mt;
+  const int Hkv = p.num_heads_kv;
+  d.HG = Hkv % 8 == 0 ? 8 : (Hkv % 4 == 0 ? 4 : (Hkv % 2 == 0 ? 2 : 1));
+  if (Hkv > 8 && d.HG != 8) return cudaErrorInvalidValue;
+  d.HGN = Hkv / d.HG;
+  d.P = NWC / d.HG;
+  d.rb_k = q8_row_bytes(D);
+  d.rb_v = p.v_fmt == G9_VFMT_Q8 ? q8_row_bytes(D) : 2 * D;
+  // dense pages: the rows of one token (all heads) are contiguous
+  if (p.k_head_stride != d.rb_k || p.k_tok_stride != (int64_t)Hkv * d.rb_k) return cudaErrorInvalidValue;
+  if (p.v_head_stride != d.rb_v || p.v_tok_stride != (int64_t)Hkv * d.rb_v) return cudaErrorInvalidValue;
+  if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.v_page_stride) & 15)
+    return cudaErrorInvalidValue;
+  auto plan_rows = [&](int rb, int64_t tok_stride, int& whole, int& stride, int& page) -> bool {
+    const int grp = d.HG * rb;
+    if (grp % 16 == 0 && tok_stride % 16 == 0) {     // one copy per token row group
+      whole = 0;
+      stride = pad_odd16(grp);
+      page = PAGE * stride;
+      return true;
+    }
+    if (d.HG == Hkv && (PAGE * grp) % 16 == 0) {     // one copy of the whole page
+      whole = 1;
+      stride = grp;
+      page = PAGE * grp;
+      return true;
+    }
+    return false;
+  };
+  if (!plan_rows(d.rb_k, p.k_tok_stride, d.k_whole, d.kstride, d.kpage)) return cudaErrorInvalidValue;
+  if (!plan_rows(d.rb_v, p.v_tok_stride, d.v_whole, d.vstride, d.vpage)) return cudaErrorInvalidValue;
+  d.stage_bytes = d.P * (d.kpage + d.vpage);
+  d.merge_off = NST * d.stage_bytes;
+  const int wph = NWC / d.HG;
+  const int merge_bytes = wph > 1 ? d.HG * mt * (16 * 4 + 4) * 32 * 4 : 0;
+  d.q_off = d.merge_off + merge_bytes;
+  d.scale_log2 = p.scale * kLog2e;
+  // chunking: enough chunks to keep every SM busy several times over
+  const int sms = num_sms();
+  const int max_pages = (p.max_kv + PAGE - 1) / PAGE;
+  const int64_t est_pages = (int64_t)p.num_seqs * d.HGN * max_pages / 2 + 1;   // lengths ~ U[0, max]
+  const int64_t want = est_pages / ((int64_t)sms * 6);
+  int cp = (int)std::min<int64_t>(std::max<int64_t>(want, 16), 512);
+  cp = ((cp + d.P - 1) / d.P) * d.P;
+  d.CP = cp;
+  d.S_max = max_pages == 0 ? 1 : (max_pages + cp - 1) / cp;
+  d.n_items = p.num_seqs * d.HGN * d.S_max;
+  return cudaSuccess;
+}
+
+static size_t decode_ws_bytes(const DecodeParams& d) {
+  const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+  const size_t o = rows * dec::D * sizeof(float);
+  return ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
+}
+
+template <int MT, int VT, bool MASK>
+static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
+  const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)d.HG * MT * 16 * dec::QROW : 0);
+  auto kern = decode_kernel<MT, VT, MASK>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int grid = std::max(1, std::min(d.n_items, num_sms()));
+  kern<<<grid, dec::NTHREADS, smem, stream>>>(d);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (d.S_max > 1) {
+    decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), dec::D, 0, stream>>>(d);
+    e = cudaGetLastError();
+  }
+  return e;
+}
+
+}  // namespace g9
+
+G9_ERROR_ACCESSORS(decode)
+
+using namespace g9;
+
+extern "C" size_t gfx906_fa_decode_workspace_size(const G9AttnBatch* batch) {
+  if (!batch) return 0;
+  DecodeParams d;
+  int mt;
+  if (plan_decode(*batch, d, mt) != cudaSuccess) return 0;
+  return decode_ws_bytes(d);
+}
+
+extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* workspace,
+                                               size_t workspace_bytes, cudaStream_t stream) {
+  if (!batch) return cudaErrorInvalidValue;
+  DecodeParams d;
+  int mt;
+  cudaError_t e = plan_decode(*batch, d, mt);
+  if (e != cudaSuccess) return e;
+  if (batch->num_seqs == 0 || batch->seq_q == 0) return cudaSuccess;
+  if (d.S_max > 1) {
+    if (!workspace || workspace_bytes < decode_ws_bytes(d) || ((uintptr_t)workspace & 15))
+      return cudaErrorInvalidValue;
+    const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+    d.opart = reinterpret_cast<float*>(workspace);
+    d.ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(workspace) +
+                                     (((rows * dec::D * sizeof(float)) + 255) & ~(size_t)255));
+  }
+  const int vt = batch->v_fmt;
+  const bool mask = batch->mask != nullptr;
+#define G9_DEC(MT_, VT_, MK_) \
+  if (mt == MT_ && vt == VT_ && mask == MK_) return launch_decode_t<MT_, VT_, MK_>(d, stream);
+  G9_DEC(1, 0, false) G9_DEC(2, 0, false) G9_DEC(1, 1, false) G9_DEC(2, 1, false)
+  G9_DEC(1, 2, false) G9_DEC(2, 2, false)
+  G9_DEC(1, 0, true) G9_DEC(2, 0, true) G9_DEC(1, 1, true) G9_DEC(2, 1, true)
+  G9_DEC(1, 2, true) G9_DEC(2, 2, true)
+#undef G9_DEC
+  return cudaErrorInvalidValue;
+}

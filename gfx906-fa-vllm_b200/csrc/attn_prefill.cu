@@ -1,0 +1,706 @@
+// attn_prefill.cu -- prefill / chunked-prefill attention on 5th-generation
+// tensor cores (tcgen05 + tensor memory), fed by TMA.
+//
+// Replaces the reference's flat tile kernel for long query chunks
+// (kernel/fattn-q8.cuh:835-1087 behind gfx906_fa_launch,
+// extension/gfx906_fa_launcher.cu:53-209, and the gather + forward pair of
+// extension/gfx906_fa_paged.py:333-445).
+//
+// Two kernels per call:
+//
+//  1. pack (CUDA cores, HBM-bound): the Q8_0 pages a prefill sequence can
+//     see are dequantised ONCE per call into fp16 staging tiles -- K as
+//     [key][d] rows, V transposed as [d][key] 128x128 tiles -- and Q is
+//     converted to fp16 with the GQA group packed into rows (row = t*G + g).
+//     Dequantisation is one rounding: q8 * d computed in fp32, rounded to
+//     fp16.  Doing it once per call instead of once per (query tile, kv
+//     tile) pair keeps the conversion work out of the tensor-core loop,
+//     where it would compete with the softmax for issue slots.
+//
+//  2. attention (tcgen05): one CTA per 128 packed query rows of one kv head.
+//     warp 0 drives TMA (128-byte swizzled tiles), warp 1 allocates tensor
+//     memory and issues tcgen05.mma from one thread, warps 4-7 run the
+//     softmax with one thread per query row (row i = TMEM lane i).  Tensor
+//     memory: S double-buffered (2 x 128 fp32 columns), O (128 columns), P
+//     double-buffered as packed fp16 (2 x 64 columns).  S = Q K^T reads both
+//     operands from shared memory; O += P V reads P from tensor memory and
+//     V^T from shared memory.  The MMA order S0 S1 PV0 S2 PV1 ... lets the
+//     next S tile run while the softmax works on the current one.  The
+//     running max is rescaled lazily (only when it grows by more than 2^8),
+//     so O in tensor memory is rarely touched by the softmax warps.
+//
+// Masking is the reference's: keys k >= kv_len ignored; causal rule
+// k <= q_abs[b] + t (fattn-q8.cuh:646-654); optional fp16 additive mask.
+// Rows without a visible key produce zeros.  All mbarrier waits are bounded.
+#include <algorithm>
+#include <cstring>
+
+#include <cuda.h>
+
+#include "attn_common.cuh"
+
+namespace g9 {
+
+namespace pf {
+constexpr int D = 128;
+constexpr int BM = 128;          // query rows per CTA
+constexpr int BN = 128;          // keys per tile
+constexpr int KST = 3;           // K smem stages
+constexpr int VST = 2;           // V smem stages
+constexpr int TILE_BYTES = BM * D * 2;   // 32 KB
+constexpr int MAXS = 128;        // prefill sequences per launch
+constexpr int NTHREADS = 256;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+}  // namespace pf
+
+struct PrefillParams {
+  CUtensorMap tm_q;
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  G9AttnBatch p;
+  int G, Hkv;
+  int nseq;
+  int min_rows;                  // sequences with n_q * G <= min_rows are left to the decode kernel
+  int RT, KT;                    // row / key tiles per head (all sequences)
+  int seq_b[pf::MAXS];
+  int rtile_off[pf::MAXS + 1];
+  int ktile_off[pf::MAXS + 1];
+  float scale_log2;
+  __half* qp;                    // [Hkv][RT*128][128]
+  __half* kp;                    // [Hkv][KT*128][128]
+  __half* vt;                    // [Hkv][KT][128 d][128 keys]
+};
+
+__device__ __forceinline__ int find_seq(const int* off, int n, int x) {
+  int lo = 0, hi = n;            // largest i with off[i] <= x
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (off[mid] <= x) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// ===========================================================================
+// pack kernels
+// ===========================================================================
+
+// K / V tile (head h, key tile kt): 128 keys of one sequence.
+__global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ PrefillParams pp) {
+  using namespace pf;
+  __shared__ __align__(16) __half vs[BN][D + 8];      // V tile, padded rows
+  const G9AttnBatch& p = pp.p;
+  const int kt = blockIdx.x;
+  const int h = blockIdx.y;
+  const int i = find_seq(pp.ktile_off, pp.nseq, kt);
+  const int j = kt - pp.ktile_off[i];
+  const int b = pp.seq_b[i];
+  if (seq_nq(p, b) * pp.G <= pp.min_rows) return;      // handled by the decode kernel
+  const int L = p.kv_len[b];
+  __half* kdst = pp.kp + ((int64_t)h * pp.KT + kt) * BN * D;
+  for (int it = threadIdx.x; it < BN * 8; it += blockDim.x) {
+    const int key_l = it >> 3;
+    const int c = it & 7;                 // 16-element chunk
+    const int key = j * BN + key_l;
+    __align__(16) __half kv[16];
+    __align__(16) __half vv[16];
+    if (key < L) {
+      const int phys = p.block_table[(int64_t)b * p.max_blocks + key / p.block_size];
+      if (phys < 0) raise_error(ERR_BAD_PAGE);
+      const int64_t off_t = (int64_t)(key % p.block_size);
+      const uint8_t* krow = p.k_cache + (int64_t)max(phys, 0) * p.k_page_stride + off_t * p.k_tok_stride +
+                            (int64_t)h * p.k_head_stride;
+      const uint8_t* kb = krow + (c >> 1) * QBLOCK;
+      const float dk = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(kb)));
+      const uint16_t* kq = reinterpret_cast<const uint16_t*>(kb + 2 + (c & 1) * 16);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint16_t w = kq[e];
+        kv[2 * e] = __float2half_rn((float)(int8_t)(w & 0xff) * dk);
+        kv[2 * e + 1] = __float2half_rn((float)(int8_t)(w >> 8) * dk);
+      }
+      const uint8_t* vrow = p.v_cache + (int64_t)max(phys, 0) * p.v_page_stride + off_t * p.v_tok_stride +
+                            (int64_t)h * p.v_head_stride;
+      if (p.v_fmt == G9_VFMT_Q8) {
+        const uint8_t* vb = vrow + (c >> 1) * QBLOCK;
+        const float dv = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(vb)));
+        const uint16_t* vq = reinterpret_cast<const uint16_t*>(vb + 2 + (c & 1) * 16);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint16_t w = vq[e];
+          vv[2 * e] = __float2half_rn((float)(int8_t)(w & 0xff) * dv);
+          vv[2 * e + 1] = __float2half_rn((float)(int8_t)(w >> 8) * dv);
+        }
+      } else if (p.v_fmt == G9_VFMT_F16) {
+        const uint32_t* v32 = reinterpret_cast<const uint32_t*>(vrow + c * 32);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) reinterpret_cast<uint32_t*>(vv)[e] = v32[e];
+      } else {   // bf16 V -> fp16 (the MMA uses fp16 for P and V)
+        const __nv_bfloat16* vb16 = reinterpret_cast<const __nv_bfloat16*>(vrow + c * 32);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) vv[e] = __float2half_rn(__bfloat162float(vb16[e]));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) kv[e] = vv[e] = __float2half_rn(0.f);
+    }
+    uint4* kd = reinterpret_cast<uint4*>(kdst + (int64_t)key_l * D + c * 16);
+    kd[0] = reinterpret_cast<uint4*>(kv)[0];
+    kd[1] = reinterpret_cast<uint4*>(kv)[1];
+    uint4* vsd = reinterpret_cast<uint4*>(&vs[key_l][c * 16]);
+    vsd[0] = reinterpret_cast<uint4*>(vv)[0];
+    vsd[1] = reinterpret_cast<uint4*>(vv)[1];
+  }
+  __syncthreads();
+  // transposed write: V^T tile [d][key], 8 keys (16 bytes) per item
+  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)D * BN;
+  for (int it = threadIdx.x; it < D * (BN / 8); it += blockDim.x) {
+    const int d = it / (BN / 8);
+    const int k8 = (it % (BN / 8)) * 8;
+    __align__(16) __half t8[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) t8[e] = vs[k8 + e][d];
+    *reinterpret_cast<uint4*>(vdst + (int64_t)d * BN + k8) = *reinterpret_cast<uint4*>(t8);
+  }
+}
+
+// Q tile (head h, row tile rt): rows r = t*G + g -> fp16.
+__global__ void __launch_bounds__(256) pack_q_kernel(const __grid_constant__ PrefillParams pp) {
+  using namespace pf;
+  const G9AttnBatch& p = pp.p;
+  const int rt = blockIdx.x;
+  const int h = blockIdx.y;
+  const int i = find_seq(pp.rtile_off, pp.nseq, rt);
+  const int m = rt - pp.rtile_off[i];
+  const int b = pp.seq_b[i];
+  const int nq = seq_nq(p, b);
+  if (nq * pp.G <= pp.min_rows) return;
+  __half* dst = pp.qp + ((int64_t)h * pp.RT + rt) * BM * D;
+  for (int it = threadIdx.x; it < BM * (D / 8); it += blockDim.x) {
+    const int r = it / (D / 8);
+    const int c8 = (it % (D / 8)) * 8;
+    const int rg = m * BM + r;
+    const int t = rg / pp.G;
+    __align__(16) __half v[8];
+    if (t < nq) {
+      const int hq = h * pp.G + (rg - t * pp.G);
+      const int64_t base = q_offset(p, b, t, hq) + c8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __float2half_rn(load_one(p.q, base + e, p.q_dtype));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = __float2half_rn(0.f);
+    }
+    *reinterpret_cast<uint4*>(dst + (int64_t)r * D + c8) = *reinterpret_cast<uint4*>(v);
+  }
+}
+
+// ===========================================================================
+// tcgen05 / TMA / TMEM wrappers
+// ===========================================================================
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(tm), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T
+__device__ __forceinline__ void tc_mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this warp's 32 lanes
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (the layout TMA writes for a box of 64 fp16 x rows).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);            // start address
+  d |= (uint64_t)1 << 16;                            // leading byte offset (unused for SW128 K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;                  // stride byte offset
+  d |= (uint64_t)1 << 46;                            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp16 A/B, fp32 D, both K-major.
+constexpr uint32_t kIdesc = (1u << 4)                       // D format f32
+                            | (0u << 7) | (0u << 10)        // A, B f16
+                            | ((uint32_t)(pf::BN >> 3) << 17)   // N
+                            | ((uint32_t)(pf::BM >> 4) << 24);  // M
+
+// ===========================================================================
+// attention kernel
+// ===========================================================================
+template <bool MASK>
+__global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams pp) {
+  using namespace pf;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + TILE_BYTES;
+  uint8_t* sV = sK + KST * TILE_BYTES;
+  __shared__ __align__(8) uint64_t bar_q;
+  __shared__ __align__(8) uint64_t bar_kfull[KST], bar_kempty[KST];
+  __shared__ __align__(8) uint64_t bar_vfull[VST], bar_vempty[VST];
+  __shared__ __align__(8) uint64_t bar_s[2];     // S tile ready (MMA -> softmax)
+  __shared__ __align__(8) uint64_t bar_p[2];     // P tile ready (softmax -> MMA)
+  __shared__ __align__(8) uint64_t bar_o[2];     // PV_j finished (barrier j & 1)
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+
+  const G9AttnBatch& p = pp.p;
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  // ---- work item: heavy (late) row tiles first --------------------------------
+  const int idx = blockIdx.x;
+  const int h = idx % pp.Hkv;
+  const int grt = pp.RT - 1 - idx / pp.Hkv;               // global row tile
+  const int si = find_seq(pp.rtile_off, pp.nseq, grt);
+  const int m = grt - pp.rtile_off[si];
+  const int b = pp.seq_b[si];
+  const int nq = seq_nq(p, b);
+  const int R = nq * pp.G;
+  const int kv_len = p.kv_len[b];
+  const int qabs = p.q_abs ? p.q_abs[b] : 0;
+  const int row0 = m * BM;
+  if (row0 >= R || R <= pp.min_rows) return;              // padding tile / decode-sized sequence
+  const int t_lo = row0 / pp.G;
+  const int t_hi = min(nq - 1, (row0 + BM - 1) / pp.G);
+  int key_end = kv_len;                                    // keys any row of the tile sees
+  int key_full = kv_len;                                   // keys every row sees
+  if (p.q_abs) {
+    key_end = min(key_end, max(0, qabs + t_hi + 1));
+    key_full = min(key_full, max(0, qabs + t_lo + 1));
+  }
+  const int nkv = (key_end + BN - 1) / BN;
+  const int q_row_g = (h * pp.RT + pp.rtile_off[si] + m) * BM;
+  const int k_row_g = (h * pp.KT + pp.ktile_off[si]) * BN;
+  const int v_tile_g = h * pp.KT + pp.ktile_off[si];
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_q, 1);
+    for (int i = 0; i < KST; ++i) { mbar_init(&bar_kfull[i], 1); mbar_init(&bar_kempty[i], 1); }
+    for (int i = 0; i < VST; ++i) { mbar_init(&bar_vfull[i], 1); mbar_init(&bar_vempty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&bar_s[i], 1); mbar_init(&bar_p[i], 128); mbar_init(&bar_o[i], 1); }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    // allocate 512 tensor-memory columns: S0 S1 (0..255), O (256..383), P0 P1 (384..511)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;"
+                 ::"r"(smem_u32(&tmem_base_sh)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+  const uint32_t tP[2] = {tmem + 384, tmem + 448};
+
+  if (nkv > 0) {
+    if (warp == 0) {
+      // ======================= TMA producer ==================================
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&bar_q, TILE_BYTES);
+        tma_load_2d(sQ, &pp.tm_q, 0, q_row_g, &bar_q);
+        tma_load_2d(sQ + TILE_BYTES / 2, &pp.tm_q, 64, q_row_g, &bar_q);
+        for (int j = 0; j < nkv; ++j) {
+          const int ks = j % KST;
+          if (j >= KST && !mbar_wait(&bar_kempty[ks], ((j / KST) - 1) & 1)) { abort_flag = 1; break; }
+          uint8_t* kd = sK + ks * TILE_BYTES;
+          mbar_arrive_expect_tx(&bar_kfull[ks], TILE_BYTES);
+          tma_load_2d(kd, &pp.tm_k, 0, k_row_g + j * BN, &bar_kfull[ks]);
+          tma_load_2d(kd + TILE_BYTES / 2, &pp.tm_k, 64, k_row_g + j * BN, &bar_kfull[ks]);
+          const int vs = j % VST;
+          if (j >= VST && !mbar_wait(&bar_vempty[vs], ((j / VST) - 1) & 1)) { abort_flag = 1; break; }
+          uint8_t* vd = sV + vs * TILE_BYTES;
+          mbar_arrive_expect_tx(&bar_vfull[vs], TILE_BYTES);
+          tma_load_2d(vd, &pp.tm_v, 0, (v_tile_g + j) * D, &bar_vfull[vs]);
+          tma_load_2d(vd + TILE_BYTES / 2, &pp.tm_v, 64, (v_tile_g + j) * D, &bar_vfull[vs]);
+        }
+      }
+    } else if (warp == 1) {
+      // ======================= MMA issuer ====================================
+      if (lane == 0) {
+        const uint32_t q_s = smem_u32(sQ);
+        auto issue_s = [&](int j) -> bool {
+          const int ks = j % KST;
+          if (!mbar_wait(&bar_kfull[ks], (j / KST) & 1)) return false;
+          tc_fence_after();
+          const uint32_t k_s = smem_u32(sK + ks * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
+            tc_mma_ss(tS[j & 1], sw128_desc(q_s + off), sw128_desc(k_s + off), kIdesc, kk > 0);
+          }
+          tc_commit(&bar_kempty[ks]);     // K stage free once this S is done
+          tc_commit(&bar_s[j & 1]);       // S tile ready
+          return true;
+        };
+        bool ok = mbar_wait(&bar_q, 0);
+        tc_fence_after();
+        ok = ok && issue_s(0);
+        if (ok && nkv > 1) ok = issue_s(1);
+        for (int j = 0; ok && j < nkv; ++j) {
+          // O += P_j V_j
+          const int vs = j % VST;
+          if (!mbar_wait(&bar_p[j & 1], (j >> 1) & 1)) { ok = false; break; }
+          if (!mbar_wait(&bar_vfull[vs], (j / VST) & 1)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t v_s = smem_u32(sV + vs * TILE_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
+            tc_mma_ts(tO, tP[j & 1] + kk * 8, sw128_desc(v_s + off), kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&bar_vempty[vs]);
+          tc_commit(&bar_o[j & 1]);
+          if (j + 2 < nkv) ok = issue_s(j + 2);
+        }
+        if (!ok) abort_flag = 1;
+      }
+    } else if (warp >= 4) {
+      // ======================= softmax (one thread per row) ==================
+      const int r = (warp - 4) * 32 + lane;                 // TMEM lane == row
+      const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+      const int rg = row0 + r;
+      const int t = rg / pp.G;
+      const bool row_valid = rg < R;
+      int row_end = kv_len;                                 // keys this row sees
+      if (p.q_abs) row_end = min(row_end, max(0, qabs + t + 1));
+      if (!row_valid) row_end = 0;
+      float m_run = -INFINITY, l_run = 0.f;
+      bool alive = true;
+      for (int j = 0; j < nkv && alive; ++j) {
+        if (!mbar_wait(&bar_s[j & 1], (j >> 1) & 1)) alive = false;
+        if (!__all_sync(0xffffffffu, alive)) { alive = false; break; }
+        tc_fence_after();
+        uint32_t s[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(tS[j & 1] + lane_off + c * 32, s[c]);
+        tmem_wait_ld();
+        const int k0 = j * BN;
+        const bool need_mask = MASK || (k0 + BN > key_full) || !row_valid;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float x = __uint_as_float(s[c][e]) * pp.scale_log2;
+            if (need_mask) {
+              const int k = k0 + c * 32 + e;
+              if constexpr (MASK) {
+                if (row_valid && k < kv_len)
+                  x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                      (int64_t)b * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+              }
+              if (k >= row_end) x = -INFINITY;
+            }
+            s[c][e] = __float_as_uint(x);
+            mx = fmaxf(mx, x);
+          }
+        // lazy rescale: keep the old max unless the new one exceeds it by
+        // more than 2^8.  tcgen05.ld/st are warp-collective, so the O
+        // rescale is decided by a warp vote; rows that do not need it scale
+        // by 1.
+        float alpha = 1.f;
+        bool rescale_o = false;
+        if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleThreshold)) {
+          if (m_run != -INFINITY) {
+            alpha = fast_exp2(m_run - mx);
+            l_run *= alpha;
+            rescale_o = j > 0;
+          }
+          m_run = mx;
+        }
+        if (__any_sync(0xffffffffu, rescale_o)) {
+          // O holds PV_0 .. PV_{j-1}; wait for PV_{j-1}, then rescale in place
+          if (!mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1)) alive = false;
+          if (!__all_sync(0xffffffffu, alive)) { alive = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + lane_off + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + lane_off + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+        const float mu = m_run == -INFINITY ? 0.f : m_run;
+        float ls = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float p0 = fast_exp2(__uint_as_float(s[c][2 * e]) - mu);
+            const float p1 = fast_exp2(__uint_as_float(s[c][2 * e + 1]) - mu);
+            ls += p0 + p1;
+            pk[e] = pack_half2(p0, p1);
+          }
+          // 16 packed columns per 32 keys
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+              ::"r"(tP[j & 1] + lane_off + c * 16), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]),
+                "r"(pk[5]), "r"(pk[6]), "r"(pk[7]), "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]),
+                "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
+              : "memory");
+        }
+        l_run += ls;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bar_p[j & 1]);
+      }
+      // ---- epilogue: O / l -> out -------------------------------------------------
+      // PV_{nkv-1} completing implies every earlier MMA completed
+      if (alive && mbar_wait(&bar_o[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1)) {
+        tc_fence_after();
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        const int g = rg - t * pp.G;
+        const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + lane_off + c * 32, o);
+          tmem_wait_ld();
+          if (row_valid) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 2)
+              store_out2(p.out, p.out_dtype, ob + c * 32 + e, __uint_as_float(o[e]) * inv,
+                         __uint_as_float(o[e + 1]) * inv);
+          }
+        }
+      } else {
+        abort_flag = 1;
+      }
+    }
+  } else if (warp >= 4) {
+    // no visible key for any row of this tile: zeros
+    const int r = (warp - 4) * 32 + lane;
+    const int rg = row0 + r;
+    if (rg < R) {
+      const int t = rg / pp.G;
+      const int64_t ob = o_offset(p, b, t, h * pp.G + (rg - t * pp.G));
+      for (int e = 0; e < D; e += 2) store_out2(p.out, p.out_dtype, ob + e, 0.f, 0.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_flag) raise_error(ERR_WAIT_TIMEOUT);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// 2-D fp16 tensor [rows][128], box 64 x 128 rows, 128-byte swizzle
+static bool make_tmap(CUtensorMap* tm, const void* base, int64_t rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)pf::D, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)pf::D * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t es[2] = {1, 1};
+  return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct PrefillPlan {
+  int RT = 0, KT = 0;
+  size_t q_bytes = 0, k_bytes = 0, v_bytes = 0, total = 0;
+};
+
+// n_q caps and kv caps are host-side upper bounds
+static PrefillPlan plan_prefill(const G9AttnBatch& p, int nseq, const int* nq_cap, const int* kv_cap) {
+  PrefillPlan pl;
+  const int G = p.num_heads_q / p.num_heads_kv;
+  for (int i = 0; i < nseq; ++i) {
+    pl.RT += (int)(((int64_t)nq_cap[i] * G + pf::BM - 1) / pf::BM);
+    pl.KT += (kv_cap[i] + pf::BN - 1) / pf::BN;
+  }
+  const size_t tile = (size_t)pf::TILE_BYTES;
+  pl.q_bytes = (size_t)p.num_heads_kv * pl.RT * tile;
+  pl.k_bytes = (size_t)p.num_heads_kv * pl.KT * tile;
+  pl.v_bytes = pl.k_bytes;
+  pl.total = pl.q_bytes + pl.k_bytes + pl.v_bytes + 1024;
+  return pl;
+}
+
+static cudaError_t check_prefill_batch(const G9AttnBatch& p) {
+  if (p.head_dim != pf::D) return cudaErrorInvalidValue;
+  if (p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv) return cudaErrorInvalidValue;
+  if (p.block_size <= 0 || p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2) return cudaErrorInvalidValue;
+  if (p.v_fmt < 0 || p.v_fmt > 2) return cudaErrorInvalidValue;
+  // K rows and Q8_0 V rows are read with 2-byte loads, 16-bit V rows with 4-byte loads
+  if (((uintptr_t)p.k_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.k_tok_stride | (uintptr_t)p.k_head_stride) & 1)
+    return cudaErrorInvalidValue;
+  const uintptr_t va = p.v_fmt == G9_VFMT_Q8 ? 1 : 3;
+  if (((uintptr_t)p.v_cache | (uintptr_t)p.v_page_stride | (uintptr_t)p.v_tok_stride | (uintptr_t)p.v_head_stride) & va)
+    return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, const int* nq_cap,
+                        const int* kv_cap, int min_rows, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  using namespace pf;
+  cudaError_t e = check_prefill_batch(p);
+  if (e != cudaSuccess) return e;
+  for (int base = 0; base < nseq; base += MAXS) {
+    const int n = std::min(MAXS, nseq - base);
+    PrefillPlan pl = plan_prefill(p, n, nq_cap + base, kv_cap + base);
+    if (pl.RT == 0) continue;
+    if (!ws || ws_bytes < pl.total) return cudaErrorInvalidValue;
+    PrefillParams pp;
+    memset(&pp, 0, sizeof(pp));
+    pp.p = p;
+    pp.G = p.num_heads_q / p.num_heads_kv;
+    pp.Hkv = p.num_heads_kv;
+    pp.nseq = n;
+    pp.min_rows = min_rows;
+    pp.scale_log2 = p.scale * kLog2e;
+    int ro = 0, ko = 0;
+    for (int i = 0; i < n; ++i) {
+      pp.seq_b[i] = seq_ids[base + i];
+      pp.rtile_off[i] = ro;
+      pp.ktile_off[i] = ko;
+      ro += (int)(((int64_t)nq_cap[base + i] * pp.G + BM - 1) / BM);
+      ko += (kv_cap[base + i] + BN - 1) / BN;
+    }
+    pp.rtile_off[n] = ro;
+    pp.ktile_off[n] = ko;
+    pp.RT = ro;
+    pp.KT = ko;
+    uint8_t* w = reinterpret_cast<uint8_t*>(((uintptr_t)ws + 1023) & ~(uintptr_t)1023);
+    pp.qp = reinterpret_cast<__half*>(w);
+    pp.kp = reinterpret_cast<__half*>(w + pl.q_bytes);
+    pp.vt = reinterpret_cast<__half*>(w + pl.q_bytes + pl.k_bytes);
+    if (!make_tmap(&pp.tm_q, pp.qp, (int64_t)pp.Hkv * pp.RT * BM) ||
+        !make_tmap(&pp.tm_k, pp.kp, (int64_t)pp.Hkv * std::max(pp.KT, 1) * BN) ||
+        !make_tmap(&pp.tm_v, pp.vt, (int64_t)pp.Hkv * std::max(pp.KT, 1) * D))
+      return cudaErrorInvalidValue;
+    if (pp.KT > 0) {
+      pack_kv_kernel<<<dim3(pp.KT, pp.Hkv), 256, 0, stream>>>(pp);
+      if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    pack_q_kernel<<<dim3(pp.RT, pp.Hkv), 256, 0, stream>>>(pp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t smem = (size_t)(1 + KST + VST) * TILE_BYTES + 1024;
+    auto kern = p.mask ? prefill_kernel<true> : prefill_kernel<false>;
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
+      return e;
+    kern<<<pp.Hkv * pp.RT, NTHREADS, smem, stream>>>(pp);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+size_t prefill_ws_bytes(const G9AttnBatch& p, int nseq, const int* nq_cap, const int* kv_cap) {
+  size_t best = 0;
+  for (int base = 0; base < nseq; base += pf::MAXS) {
+    const int n = std::min(pf::MAXS, nseq - base);
+    best = std::max(best, plan_prefill(p, n, nq_cap + base, kv_cap + base).total);
+  }
+  return best;
+}
+
+}  // namespace g9
+
+G9_ERROR_ACCESSORS(prefill)
+
+using namespace g9;
+
+extern "C" size_t gfx906_fa_prefill_workspace_size(const G9AttnBatch* batch, int num_prefill_seqs,
+                                                   const int* nq_cap, const int* kv_cap) {
+  if (!batch || num_prefill_seqs < 0 || (num_prefill_seqs > 0 && (!nq_cap || !kv_cap))) return 0;
+  if (batch->num_heads_kv <= 0 || batch->num_heads_q <= 0) return 0;
+  return prefill_ws_bytes(*batch, num_prefill_seqs, nq_cap, kv_cap);
+}
+
+extern "C" cudaError_t gfx906_fa_prefill_tc(const G9AttnBatch* batch, int num_prefill_seqs, const int* seq_ids,
+                                            const int* nq_cap, const int* kv_cap, void* workspace,
+                                            size_t workspace_bytes, cudaStream_t stream) {
+  if (!batch || num_prefill_seqs < 0) return cudaErrorInvalidValue;
+  if (num_prefill_seqs == 0) return cudaSuccess;
+  if (!seq_ids || !nq_cap || !kv_cap) return cudaErrorInvalidValue;
+  for (int i = 0; i < num_prefill_seqs; ++i)
+    if (seq_ids[i] < 0 || seq_ids[i] >= batch->num_seqs || nq_cap[i] < 0 || kv_cap[i] < 0)
+      return cudaErrorInvalidValue;
+  return run_prefill(*batch, num_prefill_seqs, seq_ids, nq_cap, kv_cap, 0, workspace, workspace_bytes, stream);
+}

@@ -7,6 +7,10 @@ cudaError_t err_get_store(unsigned int*);
 cudaError_t err_clear_store();
 cudaError_t err_get_gather(unsigned int*);
 cudaError_t err_clear_gather();
+cudaError_t err_get_decode(unsigned int*);
+cudaError_t err_clear_decode();
+cudaError_t err_get_prefill(unsigned int*);
+cudaError_t err_clear_prefill();
 }  // namespace g9
 
 extern "C" cudaError_t gfx906_fa_get_device_error(unsigned int* out) {
@@ -14,7 +18,7 @@ extern "C" cudaError_t gfx906_fa_get_device_error(unsigned int* out) {
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return e;
   unsigned int acc = 0, v = 0;
-  cudaError_t (*getters[])(unsigned int*) = {g9::err_get_store, g9::err_get_gather};
+  cudaError_t (*getters[])(unsigned int*) = {g9::err_get_store, g9::err_get_gather, g9::err_get_decode, g9::err_get_prefill};
   for (auto g : getters) {
     if ((e = g(&v)) != cudaSuccess) return e;
     acc |= v;
@@ -24,7 +28,7 @@ extern "C" cudaError_t gfx906_fa_get_device_error(unsigned int* out) {
 }
 
 extern "C" cudaError_t gfx906_fa_clear_device_error(void) {
-  cudaError_t (*clears[])() = {g9::err_clear_store, g9::err_clear_gather};
+  cudaError_t (*clears[])() = {g9::err_clear_store, g9::err_clear_gather, g9::err_clear_decode, g9::err_clear_prefill};
   for (auto c : clears) {
     cudaError_t e = c();
     if (e != cudaSuccess) return e;

@@ -106,14 +106,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each poll may suspend the
-// thread for a hardware-defined interval), records ERR_WAIT_TIMEOUT and
-// returns false.  Callers then skip the remaining work of the CTA.
-constexpr uint32_t kWaitLimit = 1u << 24;
+// Bounded wait: polls until the phase completes or about two seconds of
+// wall time (%globaltimer) have passed; on timeout it records
+// ERR_WAIT_TIMEOUT and returns false, and callers skip the remaining work of
+// the CTA.  Nothing in a correct run comes near the limit.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0 && global_ns() - t0 > kWaitLimitNs) break;
   }
   raise_error(ERR_WAIT_TIMEOUT);
   return false;

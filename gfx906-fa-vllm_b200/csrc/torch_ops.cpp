@@ -192,6 +192,286 @@ void store_kv(torch::Tensor key, torch::Tensor value, torch::Tensor slot_mapping
                "gfx906_fa_store_kv");
 }
 
+// ---------------------------------------------------------------------------
+// attention
+// ---------------------------------------------------------------------------
+G9AttnBatch batch_base(const torch::Tensor& key_cache_q8, const torch::Tensor& value_cache, int v_fmt,
+                       const torch::Tensor& block_table, const torch::Tensor& kv_len) {
+  G9AttnBatch b{};
+  const int64_t ke = key_cache_q8.element_size();
+  const int64_t ve = value_cache.element_size();
+  b.k_cache = reinterpret_cast<const uint8_t*>(key_cache_q8.data_ptr());
+  b.k_page_stride = key_cache_q8.stride(0) * ke;
+  b.k_tok_stride = key_cache_q8.stride(1) * ke;
+  b.k_head_stride = key_cache_q8.stride(2) * ke;
+  b.v_cache = reinterpret_cast<const uint8_t*>(value_cache.data_ptr());
+  b.v_page_stride = value_cache.stride(0) * ve;
+  b.v_tok_stride = value_cache.stride(1) * ve;
+  b.v_head_stride = value_cache.stride(2) * ve;
+  b.v_fmt = v_fmt;
+  b.block_table = block_table.data_ptr<int32_t>();
+  b.max_blocks = block_table.size(1);
+  b.block_size = key_cache_q8.size(1);
+  b.kv_len = kv_len.data_ptr<int32_t>();
+  b.num_seqs = block_table.size(0);
+  b.num_heads_kv = key_cache_q8.size(2);
+  return b;
+}
+
+int infer_v_fmt(const torch::Tensor& value_cache, int64_t D) {
+  if (value_cache.dtype() == torch::kUInt8) {
+    TORCH_CHECK(value_cache.size(3) == (D / 32) * 34, "Q8_0 value_cache last dim must be (D/32)*34");
+    return G9_VFMT_Q8;
+  }
+  TORCH_CHECK(value_cache.size(3) == D, "value_cache D mismatch q D");
+  if (value_cache.dtype() == torch::kFloat16) return G9_VFMT_F16;
+  TORCH_CHECK(value_cache.dtype() == torch::kBFloat16, "value_cache must be fp16, bf16 or uint8 (Q8_0)");
+  return G9_VFMT_BF16;
+}
+
+void check_paged(const torch::Tensor& key_cache_q8, const torch::Tensor& value_cache,
+                 const torch::Tensor& block_table, const torch::Tensor& seq_lens, int64_t D, int64_t B) {
+  CHECK_CUDA(key_cache_q8);
+  CHECK_CUDA(value_cache);
+  CHECK_CUDA(block_table);
+  CHECK_CUDA(seq_lens);
+  TORCH_CHECK(key_cache_q8.dtype() == torch::kUInt8, "key_cache_q8 must be uint8");
+  TORCH_CHECK(block_table.dtype() == torch::kInt32, "block_table must be int32");
+  TORCH_CHECK(seq_lens.dtype() == torch::kInt32, "seq_lens must be int32");
+  TORCH_CHECK(key_cache_q8.dim() == 4, "key_cache_q8 must be [num_blocks, block_size, Hkv, bytes_per_row]");
+  TORCH_CHECK(value_cache.dim() == 4, "value_cache must be [num_blocks, block_size, Hkv, D]");
+  TORCH_CHECK(D == 128, "head_dim must be 128");
+  TORCH_CHECK(key_cache_q8.size(3) == (D / 32) * 34, "bytes_per_row must equal (D/32)*34");
+  TORCH_CHECK(value_cache.size(0) == key_cache_q8.size(0), "value_cache blocks mismatch");
+  TORCH_CHECK(value_cache.size(1) == key_cache_q8.size(1), "value_cache block_size mismatch");
+  TORCH_CHECK(value_cache.size(2) == key_cache_q8.size(2), "value_cache Hkv mismatch");
+  TORCH_CHECK(key_cache_q8.stride(3) == 1 && value_cache.stride(3) == 1, "cache rows must be contiguous");
+  TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == B, "block_table[0] must equal batch");
+  TORCH_CHECK(seq_lens.dim() == 1 && seq_lens.size(0) == B, "seq_lens must be [batch]");
+  TORCH_CHECK(block_table.is_contiguous() && seq_lens.is_contiguous(), "block_table / seq_lens must be contiguous");
+}
+
+// Runs one batch through gfx906_fa_attention (decode and/or tensor-core
+// prefill), workspace from the caching allocator.
+void run_attention(G9AttnBatch& b, const torch::Tensor& like, const int* nq_host = nullptr,
+                   const int* kv_host = nullptr) {
+  const size_t ws = gfx906_fa_attention_workspace_size(&b, nq_host, kv_host);
+  TORCH_CHECK(ws > 0, "attention: unsupported shape");
+  auto wsbuf = torch::empty({(int64_t)ws}, like.options().dtype(torch::kUInt8));
+  check_status(gfx906_fa_attention(&b, nq_host, kv_host, wsbuf.data_ptr(), ws, cur_stream()),
+               "gfx906_fa_attention");
+}
+
+void set_mask_qabs(G9AttnBatch& b, int64_t B, int64_t Sq, int64_t min_cols, c10::optional<torch::Tensor>& mask,
+                   c10::optional<torch::Tensor>& q_abs_offset, torch::Tensor& mask_c, torch::Tensor& qo_c) {
+  TORCH_CHECK(!(mask.has_value() && q_abs_offset.has_value()),
+              "q_abs_offset and mask are mutually exclusive (inline causal replaces mask)");
+  if (mask.has_value()) {
+    auto m = mask.value();
+    CHECK_CUDA(m);
+    TORCH_CHECK(m.dtype() == torch::kFloat16, "mask must be fp16");
+    TORCH_CHECK(m.dim() == 3 && m.size(0) == B && m.size(1) == Sq, "mask must be [B, Sq, Skv_pad]");
+    TORCH_CHECK(m.size(2) >= min_cols, "mask.size(2) must cover every key (", min_cols, ")");
+    mask_c = m.contiguous();
+    b.mask = mask_c.data_ptr();
+    b.mask_seq_stride = mask_c.size(1) * mask_c.size(2);
+    b.mask_tok_stride = mask_c.size(2);
+  }
+  if (q_abs_offset.has_value()) {
+    auto qo = q_abs_offset.value();
+    CHECK_CUDA(qo);
+    TORCH_CHECK(qo.dtype() == torch::kInt32 && qo.dim() == 1 && qo.size(0) == B, "q_abs_offset must be int32 [B]");
+    qo_c = qo.contiguous();
+    b.q_abs = qo_c.data_ptr<int32_t>();
+  }
+}
+
+// forward (extension/gfx906_fa.cpp:120-265): q [B, Hq, Sq, D], k_q8
+// [B, Hkv, Skv, D/32*34], v [B, Hkv, Skv, D] -> fp32 [B, Hq, Sq, D].
+// kv_max int32 [B], mask fp16 [B, Sq, >=Skv], q_abs_offset int32 [B].
+torch::Tensor forward(torch::Tensor q, torch::Tensor k_q8, torch::Tensor v, double scale,
+                      c10::optional<torch::Tensor> kv_max, c10::optional<torch::Tensor> mask,
+                      c10::optional<torch::Tensor> q_abs_offset) {
+  CHECK_CUDA(q);
+  CHECK_CUDA(k_q8);
+  CHECK_CUDA(v);
+  CHECK_CONTIG(q);
+  CHECK_CONTIG(k_q8);
+  CHECK_CONTIG(v);
+  const int qdt = dtype_code(q, "q");
+  TORCH_CHECK(k_q8.dtype() == torch::kUInt8, "k_q8 must be uint8 (block_q8_0 bytes)");
+  TORCH_CHECK(q.dim() == 4, "q must be 4D [B, Hq, Sq, D]");
+  TORCH_CHECK(v.dim() == 4, "v_fp16 must be 4D [B, Hkv, Skv, D]");
+  const int64_t B = q.size(0), Hq = q.size(1), Sq = q.size(2), D = q.size(3);
+  const int64_t Hkv = v.size(1), Skv = v.size(2);
+  TORCH_CHECK(v.size(0) == B, "v batch mismatch");
+  TORCH_CHECK(D % 32 == 0, "head_dim must be multiple of 32");
+  TORCH_CHECK(D == 128, "head_dim must be 128");
+  TORCH_CHECK(k_q8.dim() == 4 && k_q8.size(0) == B && k_q8.size(1) == Hkv && k_q8.size(2) == Skv,
+              "k_q8 first 3 dims must match [B, Hkv, Skv]");
+  TORCH_CHECK(k_q8.size(3) == (D / 32) * 34, "k_q8 last dim = (D/32)*34 bytes");
+  TORCH_CHECK(Hq % Hkv == 0, "heads_q must be divisible by heads_kv");
+  const int vfmt = infer_v_fmt(v, D);
+  auto out = torch::empty({B, Hq, Sq, D}, q.options().dtype(torch::kFloat32));
+  if (B == 0 || Sq == 0) return out;
+  c10::cuda::CUDAGuard g(q.device());
+  const int64_t rb = (D / 32) * 34, vrow = v.size(3) * v.element_size();
+  auto ids = torch::arange(B, q.options().dtype(torch::kInt32)).view({B, 1});
+  torch::Tensor kvl;
+  if (kv_max.has_value()) {
+    auto kvm = kv_max.value();
+    CHECK_CUDA(kvm);
+    TORCH_CHECK(kvm.dtype() == torch::kInt32, "kv_max must be int32");
+    TORCH_CHECK(kvm.dim() == 1 && kvm.size(0) == B, "kv_max must be 1D [B]");
+    kvl = kvm.clamp(0, Skv).to(torch::kInt32).contiguous();
+  } else {
+    kvl = torch::full({B}, Skv, q.options().dtype(torch::kInt32));
+  }
+  G9AttnBatch b{};
+  b.q = q.data_ptr();
+  b.q_dtype = qdt;
+  b.q_seq_stride = Hq * Sq * D;
+  b.q_tok_stride = D;
+  b.q_head_stride = Sq * D;
+  b.seq_q = Sq;
+  b.out = out.data_ptr();
+  b.out_dtype = G9_DT_F32;
+  b.o_seq_stride = Hq * Sq * D;
+  b.o_tok_stride = D;
+  b.o_head_stride = Sq * D;
+  b.k_cache = k_q8.data_ptr<uint8_t>();
+  b.k_page_stride = Hkv * Skv * rb;
+  b.k_tok_stride = rb;
+  b.k_head_stride = Skv * rb;
+  b.v_cache = reinterpret_cast<const uint8_t*>(v.data_ptr());
+  b.v_page_stride = Hkv * Skv * vrow;
+  b.v_tok_stride = vrow;
+  b.v_head_stride = Skv * vrow;
+  b.v_fmt = vfmt;
+  b.block_table = ids.data_ptr<int32_t>();
+  b.max_blocks = 1;
+  b.block_size = std::max<int64_t>(Skv, 1);
+  b.kv_len = kvl.data_ptr<int32_t>();
+  b.max_kv = Skv;
+  b.num_seqs = B;
+  b.num_heads_q = Hq;
+  b.num_heads_kv = Hkv;
+  b.head_dim = D;
+  b.scale = (float)scale;
+  torch::Tensor mask_c, qo_c;
+  set_mask_qabs(b, B, Sq, Skv, mask, q_abs_offset, mask_c, qo_c);
+  // contiguous [B, Hkv, Skv, row] tensors are not 16-token pages: the batch
+  // goes to the tensor-core path, whose pack step reads any row layout
+  run_attention(b, q);
+  return out;
+}
+
+// forward_paged_direct (extension/gfx906_fa.cpp:516-658): q [B, Hq, Sq, D]
+// (fp32 as in the reference; fp16 / bf16 also accepted) -> fp32 [B, Hq, Sq, D].
+torch::Tensor forward_paged_direct(torch::Tensor q, torch::Tensor key_cache_q8, torch::Tensor value_cache,
+                                   torch::Tensor block_table, torch::Tensor seq_lens, double scale,
+                                   c10::optional<torch::Tensor> mask, c10::optional<torch::Tensor> q_abs_offset) {
+  CHECK_CUDA(q);
+  CHECK_CONTIG(q);
+  TORCH_CHECK(q.dim() == 4, "q must be 4D [B, Hq, Sq, D]");
+  const int qdt = dtype_code(q, "q");
+  const int64_t B = q.size(0), Hq = q.size(1), Sq = q.size(2), D = q.size(3);
+  check_paged(key_cache_q8, value_cache, block_table, seq_lens, D, B);
+  const int vfmt = infer_v_fmt(value_cache, D);
+  TORCH_CHECK(key_cache_q8.size(1) == 16, "Only block_size=16 supported, got ", key_cache_q8.size(1));
+  TORCH_CHECK(Hq % key_cache_q8.size(2) == 0, "heads_q must be divisible by heads_kv");
+  auto out = torch::empty({B, Hq, Sq, D}, q.options().dtype(torch::kFloat32));
+  if (B == 0 || Sq == 0) return out;
+  c10::cuda::CUDAGuard g(q.device());
+  G9AttnBatch b = batch_base(key_cache_q8, value_cache, vfmt, block_table, seq_lens);
+  b.q = q.data_ptr();
+  b.q_dtype = qdt;
+  b.q_seq_stride = Hq * Sq * D;
+  b.q_tok_stride = D;
+  b.q_head_stride = Sq * D;
+  b.seq_q = Sq;
+  b.out = out.data_ptr();
+  b.out_dtype = G9_DT_F32;
+  b.o_seq_stride = Hq * Sq * D;
+  b.o_tok_stride = D;
+  b.o_head_stride = Sq * D;
+  b.max_kv = b.max_blocks * b.block_size;
+  b.num_heads_q = Hq;
+  b.head_dim = D;
+  b.scale = (float)scale;
+  torch::Tensor mask_c, qo_c;
+  set_mask_qabs(b, B, Sq, b.max_kv, mask, q_abs_offset, mask_c, qo_c);
+  run_attention(b, q);
+  return out;
+}
+
+// paged_attention: vLLM-layout entry.  query [T, Hq, D] (fp16/bf16/fp32),
+// caches as [NB, bs, Hkv, row] views (any strides with contiguous rows),
+// query_start_loc int32 [B+1], seq_lens int32 [B].  Causal with
+// q_abs = seq_len - n_q (vLLM's chunked-prefill convention).  Writes `out`
+// [T, Hq, D] (allocated in the query dtype when not given).  Optional host
+// lists give exact query lengths / context-length bounds for routing.
+torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, torch::Tensor value_cache,
+                              torch::Tensor block_table, torch::Tensor seq_lens, torch::Tensor query_start_loc,
+                              int64_t max_query_len, int64_t max_seq_len, double scale,
+                              c10::optional<torch::Tensor> out_opt,
+                              c10::optional<std::vector<int64_t>> query_lens_host,
+                              c10::optional<std::vector<int64_t>> seq_lens_host) {
+  CHECK_CUDA(query);
+  CHECK_CUDA(query_start_loc);
+  TORCH_CHECK(query.dim() == 3 && query.stride(2) == 1, "query must be [T, Hq, D] with contiguous D");
+  const int qdt = dtype_code(query, "query");
+  const int64_t T = query.size(0), Hq = query.size(1), D = query.size(2);
+  const int64_t B = block_table.size(0);
+  check_paged(key_cache_q8, value_cache, block_table, seq_lens, D, B);
+  TORCH_CHECK(query_start_loc.dtype() == torch::kInt32 && query_start_loc.dim() == 1 &&
+                  query_start_loc.size(0) == B + 1 && query_start_loc.is_contiguous(),
+              "query_start_loc must be int32 [B+1]");
+  TORCH_CHECK(Hq % key_cache_q8.size(2) == 0, "heads_q must be divisible by heads_kv");
+  const int vfmt = infer_v_fmt(value_cache, D);
+  torch::Tensor out;
+  if (out_opt.has_value()) {
+    out = out_opt.value();
+    CHECK_CUDA(out);
+    TORCH_CHECK(out.dim() == 3 && out.size(0) >= T && out.size(1) == Hq && out.size(2) == D && out.stride(2) == 1,
+                "out must be [>=T, Hq, D] with contiguous D");
+  } else {
+    out = torch::empty({T, Hq, D}, query.options());
+  }
+  if (B == 0 || T == 0) return out;
+  c10::cuda::CUDAGuard g(query.device());
+  auto n_q = (query_start_loc.slice(0, 1, B + 1) - query_start_loc.slice(0, 0, B)).to(torch::kInt32);
+  auto q_abs = (seq_lens - n_q).to(torch::kInt32);
+  G9AttnBatch b = batch_base(key_cache_q8, value_cache, vfmt, block_table, seq_lens);
+  b.q = query.data_ptr();
+  b.q_dtype = qdt;
+  b.q_tok_stride = query.stride(0);
+  b.q_head_stride = query.stride(1);
+  b.q_start = query_start_loc.data_ptr<int32_t>();
+  b.n_q = n_q.data_ptr<int32_t>();
+  b.seq_q = (int)max_query_len;
+  b.out = out.data_ptr();
+  b.out_dtype = dtype_code(out, "out");
+  b.o_tok_stride = out.stride(0);
+  b.o_head_stride = out.stride(1);
+  b.max_kv = (int)max_seq_len;
+  b.q_abs = q_abs.data_ptr<int32_t>();
+  b.num_heads_q = Hq;
+  b.head_dim = D;
+  b.scale = (float)scale;
+  std::vector<int> nqh, kvh;
+  if (query_lens_host.has_value()) {
+    TORCH_CHECK((int64_t)query_lens_host->size() == B, "query_lens_host must have num_seqs entries");
+    for (auto x : *query_lens_host) nqh.push_back((int)x);
+  }
+  if (seq_lens_host.has_value()) {
+    TORCH_CHECK((int64_t)seq_lens_host->size() == B, "seq_lens_host must have num_seqs entries");
+    for (auto x : *seq_lens_host) kvh.push_back((int)x);
+  }
+  run_attention(b, query, nqh.empty() ? nullptr : nqh.data(), kvh.empty() ? nullptr : kvh.data());
+  return out;
+}
+
 unsigned int device_error(bool clear) {
   unsigned int v = 0;
   check_status(gfx906_fa_get_device_error(&v), "gfx906_fa_get_device_error");
@@ -218,6 +498,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Fused KV store by slot_mapping: K -> Q8_0, V copied (v_mode=1) or quantized (v_mode=2)",
         py::arg("key"), py::arg("value"), py::arg("slot_mapping"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("v_mode") = 1);
+  m.def("forward", &forward, "FA forward (Q fp32/fp16/bf16, K q8_0, V fp16): fp32 [B, Hq, Sq, D]",
+        py::arg("q"), py::arg("k_q8"), py::arg("v_fp16"), py::arg("scale"), py::arg("kv_max") = c10::nullopt,
+        py::arg("mask") = c10::nullopt, py::arg("q_abs_offset") = c10::nullopt);
+  m.def("forward_paged_direct", &forward_paged_direct,
+        "Direct-paged flash attention (no gather): q [B, Hq, Sq, D] -> fp32 [B, Hq, Sq, D]",
+        py::arg("q"), py::arg("key_cache_q8"), py::arg("value_cache"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("scale"), py::arg("mask") = c10::nullopt,
+        py::arg("q_abs_offset") = c10::nullopt);
+  m.def("paged_attention", &paged_attention,
+        "Varlen causal paged attention in vLLM layout: query [T, Hq, D] -> out [T, Hq, D]",
+        py::arg("query"), py::arg("key_cache_q8"), py::arg("value_cache"), py::arg("block_table"),
+        py::arg("seq_lens"), py::arg("query_start_loc"), py::arg("max_query_len"), py::arg("max_seq_len"),
+        py::arg("scale"), py::arg("out") = c10::nullopt, py::arg("query_lens_host") = c10::nullopt,
+        py::arg("seq_lens_host") = c10::nullopt);
   m.def("device_error", &device_error, "Read (and optionally clear) the library's device error word",
         py::arg("clear") = false);
 }

@@ -1,0 +1,312 @@
+# SPDX-License-Identifier: Apache-2.0
+"""vLLM v1 attention backend on the sm_100a paged-Q8 kernels.
+
+Same plugin surface as the reference (extension/gfx906_fa_backend.py of
+nick413-bit/gfx906-fa-vllm): registered as AttentionBackendEnum.CUSTOM by
+`register()` (entry point `vllm.general_plugins: gfx906_fa =
+gfx906_fa_backend:register`), the same class names, and the same KV-cache
+shape as TritonAttentionBackend, (num_blocks, 2, block_size, num_kv_heads,
+head_size), so the vLLM allocator is untouched.
+
+Differences in how the cache is used:
+  * The Q8_0 K rows live INSIDE the K half of each page of that allocation,
+    densely packed as [block_size][Hkv][D/32*34] bytes at its start (136 of
+    every 256 bytes at D = 128), written by one fused store kernel together
+    with V.  There is no separate side buffer, so nothing can fall out of
+    sync with it (the reference's side buffer did:
+    tests/test_backend_vs_legacy.py).  Consequence: vLLM code that copies K
+    pages as opaque bytes keeps working, code that reads K as 16-bit values
+    does not.
+  * V stays in the model dtype (GFX906_FA_V_FMT=fp16, default, the
+    reference's numerics) or is stored as Q8_0 at the start of the V half
+    (GFX906_FA_V_FMT=q8_0).
+  * forward writes straight into vLLM's output buffer in the model dtype:
+    no fp32 upcast of the query, no padding, no per-sequence host loop.
+  * GFX906_FA_LEGACY=1 keeps the reference's legacy design: 16-bit K/V in
+    the cache (vLLM's own reshape_and_cache_flash) and K quantised on the
+    fly in every forward.
+"""
+from __future__ import annotations
+
+import os as _os
+from dataclasses import dataclass, field
+from typing import ClassVar
+
+import torch
+
+from vllm.config import VllmConfig
+from vllm.config.cache import CacheDType
+from vllm.logger import init_logger
+from vllm.platforms.interface import DeviceCapability
+from vllm.v1.attention.backend import (
+    AttentionBackend,
+    AttentionCGSupport,
+    AttentionImpl,
+    AttentionLayer,
+    AttentionMetadataBuilder,
+    AttentionType,
+    CommonAttentionMetadata,
+    MultipleOf,
+)
+from vllm.v1.kv_cache_interface import AttentionSpec
+
+import gfx906_fa
+from gfx906_fa_paged import forward_paged  # noqa: E402
+
+logger = init_logger(__name__)
+
+_V_FMT = _os.environ.get("GFX906_FA_V_FMT", "fp16").lower()
+
+
+def q8_row_bytes(head_size: int) -> int:
+    return (head_size // 32) * 34
+
+
+def kv_cache_views(kv_cache: torch.Tensor, v_fmt: str = "fp16"):
+    """Views of one vLLM KV allocation [NB, 2, bs, Hkv, D] (16-bit):
+
+    k_q8: uint8 [NB, bs, Hkv, D/32*34] -- dense Q8_0 rows at the start of
+          each page's K half;
+    v:    the V half [NB, bs, Hkv, D] (fp16 mode) or uint8
+          [NB, bs, Hkv, D/32*34] at the start of each page's V half (q8_0).
+    """
+    NB, two, bs, Hkv, D = kv_cache.shape
+    rb = q8_row_bytes(D)
+    page = bs * Hkv * D * kv_cache.element_size()
+    raw = kv_cache.view(torch.uint8).view(NB, 2, page)
+    k_q8 = raw[:, 0, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
+    if v_fmt == "q8_0":
+        v = raw[:, 1, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
+    else:
+        v = kv_cache[:, 1]
+    return k_q8, v
+
+
+# -----------------------------------------------------------------------------
+# Metadata
+# -----------------------------------------------------------------------------
+@dataclass
+class Gfx906FAMetadata:
+    num_actual_tokens: int
+    max_query_len: int
+    max_seq_len: int
+    query_start_loc: torch.Tensor      # [B+1] int32
+    seq_lens: torch.Tensor             # [B]   int32
+    block_table: torch.Tensor          # [B, max_num_blocks] int32
+    slot_mapping: torch.Tensor         # [num_tokens] int64
+    use_cascade: bool = False
+    common_prefix_len: int = 0
+    # host copies made once per step by the builder (shared by every layer):
+    # exact query lengths and upper bounds of the context lengths
+    query_lens_host: list | None = field(default=None)
+    seq_lens_host: list | None = field(default=None)
+
+
+class Gfx906FAMetadataBuilder(AttentionMetadataBuilder[Gfx906FAMetadata]):
+    _cudagraph_support: ClassVar[AttentionCGSupport] = AttentionCGSupport.NEVER
+
+    def __init__(self, kv_cache_spec: AttentionSpec, layer_names: list[str], vllm_config: VllmConfig,
+                 device: torch.device):
+        super().__init__(kv_cache_spec, layer_names, vllm_config, device)
+        self.block_size = kv_cache_spec.block_size
+
+    def build_for_cudagraph_capture(self, common_attn_metadata: CommonAttentionMetadata) -> Gfx906FAMetadata:
+        return self.build(0, common_attn_metadata)
+
+    def build(self, common_prefix_len: int, common_attn_metadata: CommonAttentionMetadata,
+              fast_build: bool = False) -> Gfx906FAMetadata:
+        m = common_attn_metadata
+        qlens = slens = None
+        qsl_cpu = getattr(m, "query_start_loc_cpu", None)
+        if qsl_cpu is not None:
+            q = qsl_cpu.tolist()
+            qlens = [q[i + 1] - q[i] for i in range(len(q) - 1)]
+        ub = getattr(m, "seq_lens_cpu_upper_bound", None)
+        if ub is not None:
+            slens = ub.tolist()
+        return Gfx906FAMetadata(
+            num_actual_tokens=m.num_actual_tokens,
+            max_query_len=m.max_query_len,
+            max_seq_len=m.max_seq_len,
+            query_start_loc=m.query_start_loc,
+            seq_lens=m.seq_lens,
+            block_table=m.block_table_tensor,
+            slot_mapping=m.slot_mapping,
+            use_cascade=(common_prefix_len > 0),
+            common_prefix_len=common_prefix_len,
+            query_lens_host=qlens,
+            seq_lens_host=slens,
+        )
+
+
+# -----------------------------------------------------------------------------
+# Backend
+# -----------------------------------------------------------------------------
+class Gfx906FABackend(AttentionBackend):
+    accept_output_buffer: bool = True
+    supported_dtypes: ClassVar[list[torch.dtype]] = [torch.float16, torch.bfloat16]
+    supported_kv_cache_dtypes: ClassVar[list[CacheDType]] = ["auto", "float16", "half", "bfloat16"]
+    forward_includes_kv_cache_update: bool = False
+
+    @staticmethod
+    def get_supported_kernel_block_sizes() -> list[int | MultipleOf]:
+        return [MultipleOf(16)]
+
+    @classmethod
+    def supports_block_size(cls, block_size: int | None) -> bool:
+        if block_size is None:
+            return True
+        return block_size % 16 == 0
+
+    @staticmethod
+    def get_name() -> str:
+        return "CUSTOM"
+
+    @staticmethod
+    def get_impl_cls() -> type["Gfx906FAImpl"]:
+        return Gfx906FAImpl
+
+    @staticmethod
+    def get_kv_cache_shape(num_blocks: int, block_size: int, num_kv_heads: int, head_size: int,
+                           cache_dtype_str: str = "auto") -> tuple[int, ...]:
+        if block_size % 16 != 0:
+            raise ValueError("Block size must be a multiple of 16.")
+        return (num_blocks, 2, block_size, num_kv_heads, head_size)
+
+    @staticmethod
+    def get_kv_cache_stride_order(include_num_layers_dimension: bool = False) -> tuple[int, ...]:
+        if include_num_layers_dimension:
+            return (1, 0, 2, 3, 4, 5)
+        return (0, 1, 2, 3, 4)
+
+    @staticmethod
+    def use_cascade_attention(*args, **kwargs) -> bool:
+        return False
+
+    @staticmethod
+    def get_builder_cls() -> type["Gfx906FAMetadataBuilder"]:
+        return Gfx906FAMetadataBuilder
+
+    @classmethod
+    def supports_head_size(cls, head_size: int) -> bool:
+        return head_size == 128
+
+    @classmethod
+    def supports_mm_prefix(cls) -> bool:
+        return False
+
+    @classmethod
+    def supports_sink(cls) -> bool:
+        return False
+
+    @classmethod
+    def supports_attn_type(cls, attn_type: str) -> bool:
+        return attn_type == AttentionType.DECODER
+
+    @classmethod
+    def supports_alibi_sqrt(cls) -> bool:
+        return False
+
+    @classmethod
+    def supports_compute_capability(cls, capability: DeviceCapability) -> bool:
+        return capability.major == 10
+
+
+# -----------------------------------------------------------------------------
+# Impl
+# -----------------------------------------------------------------------------
+class Gfx906FAImpl(AttentionImpl):
+
+    def __init__(self, num_heads: int, head_size: int, scale: float, num_kv_heads: int,
+                 alibi_slopes: list[float] | None, sliding_window: int | None, kv_cache_dtype: str,
+                 logits_soft_cap: float | None = None, attn_type: AttentionType = AttentionType.DECODER,
+                 kv_sharing_target_layer_name: int | None = None, sinks: torch.Tensor | None = None,
+                 use_alibi_sqrt: bool = False) -> None:
+        if alibi_slopes is not None:
+            raise NotImplementedError("GFX906_FA: alibi_slopes is not supported")
+        if sliding_window is not None:
+            raise NotImplementedError("GFX906_FA: sliding_window is not supported")
+        if logits_soft_cap not in (None, 0, 0.0):
+            raise NotImplementedError("GFX906_FA: logits_soft_cap is not supported")
+        if sinks is not None:
+            raise NotImplementedError("GFX906_FA: sinks are not supported")
+        if attn_type != AttentionType.DECODER:
+            raise NotImplementedError(f"GFX906_FA: attn_type={attn_type} is not supported")
+        if head_size != 128:
+            raise NotImplementedError("GFX906_FA: head_size must be 128")
+        self.num_heads = num_heads
+        self.head_size = head_size
+        self.scale = float(scale)
+        self.num_kv_heads = num_kv_heads
+        self.kv_cache_dtype = kv_cache_dtype
+        self.attn_type = attn_type
+        self.kv_sharing_target_layer_name = kv_sharing_target_layer_name
+        self.num_queries_per_kv = num_heads // num_kv_heads
+        self._legacy = _os.environ.get("GFX906_FA_LEGACY", "0") == "1"
+        self._v_fmt = "q8_0" if _V_FMT in ("q8", "q8_0") else "fp16"
+
+    def fused_output_quant_supported(self, quant_key):
+        return False
+
+    def fused_rope_kvcache_supported(self):
+        return False
+
+    # ------------------------------------------------------------------
+    # KV cache write
+    # ------------------------------------------------------------------
+    def do_kv_cache_update(self, layer: AttentionLayer, key: torch.Tensor, value: torch.Tensor,
+                           kv_cache: torch.Tensor, slot_mapping: torch.Tensor):
+        slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
+        if self._legacy:
+            key_cache, value_cache = kv_cache.unbind(1)
+            torch.ops._C_cache_ops.reshape_and_cache_flash(
+                key, value, key_cache, value_cache, slots, self.kv_cache_dtype, layer._k_scale, layer._v_scale)
+            return
+        n = slots.shape[0]
+        k_q8, v = kv_cache_views(kv_cache, self._v_fmt)
+        gfx906_fa.store_kv(key[:n], value[:n], slots, k_q8, v, 2 if self._v_fmt == "q8_0" else 1)
+
+    # ------------------------------------------------------------------
+    # Forward
+    # ------------------------------------------------------------------
+    def forward(self, layer: torch.nn.Module, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                kv_cache: torch.Tensor, attn_metadata: Gfx906FAMetadata, output: torch.Tensor | None = None,
+                output_scale: torch.Tensor | None = None,
+                output_block_scale: torch.Tensor | None = None) -> torch.Tensor:
+        assert output is not None, "Output tensor must be provided."
+        if output_scale is not None or output_block_scale is not None:
+            raise NotImplementedError("GFX906_FA: output quantization is not supported")
+        if attn_metadata is None:
+            return output.fill_(0)                 # profiling run
+        assert not attn_metadata.use_cascade, "GFX906_FA: cascade attention is not supported"
+        n = attn_metadata.num_actual_tokens
+        q = query[:n]
+        out = output[:n].view(n, self.num_heads, self.head_size)
+        if self._legacy:
+            key_cache, value_cache = kv_cache.unbind(1)
+            res = forward_paged(q, key_cache, value_cache, attn_metadata.block_table, attn_metadata.seq_lens,
+                                attn_metadata.query_start_loc, attn_metadata.max_query_len,
+                                attn_metadata.max_seq_len, scale=self.scale, key_cache_q8=None)
+            out.copy_(res.view(n, self.num_heads, self.head_size))
+            return output
+        k_q8, v = kv_cache_views(kv_cache, self._v_fmt)
+        forward_paged(q, None, v, attn_metadata.block_table, attn_metadata.seq_lens,
+                      attn_metadata.query_start_loc, attn_metadata.max_query_len, attn_metadata.max_seq_len,
+                      scale=self.scale, key_cache_q8=k_q8, out=out,
+                      query_lens_host=attn_metadata.query_lens_host, seq_lens_host=attn_metadata.seq_lens_host)
+        return output
+
+
+# -----------------------------------------------------------------------------
+# Registration as AttentionBackendEnum.CUSTOM
+# -----------------------------------------------------------------------------
+def register() -> None:
+    """Register Gfx906FABackend as AttentionBackendEnum.CUSTOM (reference:
+    extension/gfx906_fa_backend.py:536-549).  Called by vLLM's general-plugin
+    loader in every process, and once more on import."""
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum, register_backend
+    register_backend(AttentionBackendEnum.CUSTOM, f"{__name__}.Gfx906FABackend")
+    logger.info("GFX906_FA backend registered as AttentionBackendEnum.CUSTOM")
+
+
+register()

@@ -95,6 +95,139 @@ cudaError_t gfx906_fa_store_kv(const void* key, int key_dtype, int64_t key_token
                                int64_t v_head_stride, int v_mode, int num_tokens, int num_kv_heads,
                                int head_size, int block_size, cudaStream_t stream);
 
+/* ----------------------------------------------------------------------- */
+/* Attention over a batch of sequences                                       */
+/* ----------------------------------------------------------------------- */
+
+/* V cache formats */
+#define G9_VFMT_F16 0
+#define G9_VFMT_BF16 1
+#define G9_VFMT_Q8 2
+
+/* One attention call.  All pointers are device pointers.
+ *
+ * Query row (sequence b, token t < n_q[b], query head hq) is read at
+ *   q + b*q_seq_stride + (q_start[b] + t)*q_tok_stride + hq*q_head_stride
+ * (elements of q_dtype) and its output written at the same position of
+ * `out` with the o_* strides (elements of out_dtype).  q_start == NULL means
+ * 0, n_q == NULL means seq_q for every sequence; seq_q is also the maximum
+ * of n_q.
+ *
+ * Key / value row (sequence b, key k < kv_len[b], kv head h) lives in page
+ * block_table[b*max_blocks + k/block_size] at
+ *   page*page_stride + (k%block_size)*tok_stride + h*head_stride   (bytes).
+ * K rows are Q8_0 (head_dim/32*34 bytes); V rows are fp16 / bf16 or Q8_0
+ * (v_fmt).  max_kv is a host-side upper bound of kv_len.
+ *
+ * Visibility: key k is visible to query token t iff k < kv_len[b] and, when
+ * q_abs != NULL, k <= q_abs[b] + t (the reference's inline causal rule,
+ * kernel/fattn-q8.cuh:646-654).  `mask` (optional, fp16, additive) adds
+ * mask[b*mask_seq_stride + t*mask_tok_stride + k] to the scaled score
+ * (kernel/fattn-q8.cuh:628-631).  Query heads map to kv heads by
+ * hq / (num_heads_q / num_heads_kv).  A query row with no visible key is
+ * written as zeros. */
+typedef struct G9AttnBatch {
+  const void* q;
+  int q_dtype;
+  int64_t q_seq_stride, q_tok_stride, q_head_stride;
+  const int32_t* q_start;
+  const int32_t* n_q;
+  int seq_q;
+  void* out;
+  int out_dtype;
+  int64_t o_seq_stride, o_tok_stride, o_head_stride;
+  const uint8_t* k_cache;
+  int64_t k_page_stride, k_tok_stride, k_head_stride;
+  const uint8_t* v_cache;
+  int64_t v_page_stride, v_tok_stride, v_head_stride;
+  int v_fmt;
+  const int32_t* block_table;
+  int max_blocks;
+  int block_size;
+  const int32_t* kv_len;
+  int max_kv;
+  const int32_t* q_abs;
+  const void* mask;
+  int64_t mask_seq_stride, mask_tok_stride;
+  int num_seqs, num_heads_q, num_heads_kv, head_dim;
+  float scale;
+} G9AttnBatch;
+
+/* Split-K flash decoding straight from the paged Q8 cache (no gather):
+ * persistent CTAs walk (KV chunk, kv-head group, sequence) items, stream
+ * whole pages into shared memory with bulk-async copies and compute all query
+ * heads of a GQA group (and all query tokens) together on tensor cores; a
+ * second kernel merges per-chunk partial results.  Handles the sequences
+ * whose GQA-packed query rows n_q * (Hq/Hkv) fit in min(32, seq_q*Hq/Hkv);
+ * others are skipped.  Requirements: head_dim 128, block_size 16,
+ * num_heads_kv in {1, 2, 4} or a multiple of 8, pages laid out
+ * [block_size][Hkv][row] (dense rows), 16-byte aligned pages.
+ * gfx906_fa_decode_workspace_size returns 0 when the batch is not supported.
+ * workspace: device scratch of at least that many bytes (16-byte aligned);
+ * its contents need no initialisation. */
+size_t gfx906_fa_decode_workspace_size(const G9AttnBatch* batch);
+cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* workspace, size_t workspace_bytes,
+                                    cudaStream_t stream);
+
+/* Tensor-core prefill: for each listed sequence (seq_ids[i], up to nq_cap[i]
+ * query tokens, up to kv_cap[i] visible keys -- host-side upper bounds) the
+ * visible Q8 pages are dequantised once into fp16 staging tiles in the
+ * workspace, then one CTA per 128 GQA-packed query rows of a kv head runs
+ * S = Q K^T and O += P V on tcgen05 tensor cores with the accumulators in
+ * tensor memory, fed by TMA.  Requirements: head_dim 128, K rows readable
+ * with 2-byte loads, 16-bit V rows with 4-byte loads.  This entry computes
+ * every listed sequence (gfx906_fa_attention leaves the short ones to the
+ * decode kernel).  workspace: at least gfx906_fa_prefill_workspace_size()
+ * bytes; no initialisation needed. */
+size_t gfx906_fa_prefill_workspace_size(const G9AttnBatch* batch, int num_prefill_seqs, const int* nq_cap,
+                                        const int* kv_cap);
+cudaError_t gfx906_fa_prefill_tc(const G9AttnBatch* batch, int num_prefill_seqs, const int* seq_ids,
+                                 const int* nq_cap, const int* kv_cap, void* workspace, size_t workspace_bytes,
+                                 cudaStream_t stream);
+
+/* Whole-batch attention: sequences whose GQA-packed query rows
+ * (n_q * Hq/Hkv) fit in 32 run on the split-K decode kernel, longer query
+ * chunks on the tensor-core prefill kernel; both read the same paged Q8
+ * cache.  nq_host / kv_host (host arrays of num_seqs ints, optional) give
+ * exact per-sequence query counts and upper bounds of the KV lengths -- with
+ * them the routing is decided on the host and the workspace is sized
+ * exactly; without them seq_q / max_kv bound every sequence and each kernel
+ * picks its sequences on the device.  The same nq_host / kv_host must be
+ * passed to the size query and to the call.  Replaces the path choice of
+ * forward_paged (extension/gfx906_fa_paged.py:60-70,255-376). */
+size_t gfx906_fa_attention_workspace_size(const G9AttnBatch* batch, const int* nq_host, const int* kv_host);
+cudaError_t gfx906_fa_attention(const G9AttnBatch* batch, const int* nq_host, const int* kv_host, void* workspace,
+                                size_t workspace_bytes, cudaStream_t stream);
+
+/* Reference flat attention: Q fp32 [B, Hq, Sq, D], K_q8 [B, Hkv, Skv,
+ * D/32*34], V fp16 [B, Hkv, Skv, D] -> O fp32 [B, Sq, Hq, D] (BSHD, as the
+ * reference kernel writes it).  KV_max: int32 [B, grid_x] as expanded by the
+ * reference's C++ (one value per sequence, repeated per query tile) or NULL;
+ * MASK_f16: additive fp16 [B, Sq, mask_seq_kv_padded] or NULL;
+ * Q_ABS_OFFSET_d: int32 [B] inline-causal offsets or NULL (exclusive with
+ * the mask).  O_meta is accepted and not written (the reference only writes
+ * it with KV splitting, which it never enables).  head_dim must be 128.
+ * Allocates its workspace with cudaMallocAsync on `stream` and frees it the
+ * same way.  Replaces gfx906_fa_launch (extension/gfx906_fa_launcher.cu:53-75). */
+cudaError_t gfx906_fa_launch(const float* Q_fp32, const void* K_q8, const void* V_f16, float* O_fp32, void* O_meta,
+                             const int* KV_max_d, const void* MASK_f16, int32_t mask_seq_kv_padded,
+                             const int32_t* Q_ABS_OFFSET_d, int batch, int heads_q, int heads_kv, int seq_q,
+                             int seq_kv, int head_dim, float scale, cudaStream_t stream);
+
+/* Reference direct-paged attention: Q fp32 [B, Hq, Sq, D] against K_paged
+ * [NB, 16, Hkv, D/32*34] / fp16 V_paged [NB, 16, Hkv, D] (byte strides)
+ * through block_table -> O fp32 [B, Sq, Hq, D] (BSHD).  kv_max_d: int32
+ * [B, grid_x] expanded per-sequence lengths (gfx906_fa.cpp:604).  Same
+ * workspace behaviour as gfx906_fa_launch.  Replaces gfx906_fa_launch_paged
+ * (extension/gfx906_fa_launcher.cu:222-249). */
+cudaError_t gfx906_fa_launch_paged(const float* Q_fp32, const void* K_paged, const void* V_paged,
+                                   const int32_t* block_table, const int32_t* kv_max_d, float* O_fp32, void* O_meta,
+                                   const void* MASK_f16, int32_t mask_seq_kv_padded, const int32_t* Q_ABS_OFFSET_d,
+                                   int batch, int heads_q, int heads_kv, int seq_q, int max_seq_kv, int head_dim,
+                                   int block_size, int max_blocks_per_seq, int64_t k_block_stride,
+                                   int64_t k_token_stride, int64_t k_head_stride, int64_t v_block_stride,
+                                   int64_t v_token_stride, int64_t v_head_stride, float scale, cudaStream_t stream);
+
 /* Device error word (bit 0: a bounded wait timed out, bit 1: a block-table
  * entry was out of range, bit 2: tensor-memory allocation failed).
  * gfx906_fa_get_device_error synchronises the current device and reads it;

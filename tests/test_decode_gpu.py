@@ -1,0 +1,156 @@
+"""Split-K decode attention straight from the paged Q8 cache, against the
+fp32 dequant + softmax oracle (tolerance |d| <= 2e-3 + 1e-2 |ref|).
+
+Cases follow the reference's own attention tests: batched decode with GQA
+48/8 and mixed context lengths (tests/test_decode_batch.py), the per-rank
+TP=8 slice Hq/Hkv = 6/1 (tests/test_fa_mixed_batch.py), inline-causal
+chunks via q_abs_offset (tests/test_inline_causal.py), plus the edges the
+reference leaves undefined (empty sequences, holes in lengths)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from _paged import PagedCase, assert_close
+from _util import to_np
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _gfx():
+    import gfx906_fa
+    return gfx906_fa
+
+
+def _q(shape, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(shape, generator=g).to(dtype)
+
+
+def _qnp(q):
+    return (to_np(q), "bf16") if q.dtype == torch.bfloat16 else (to_np(q), None)
+
+
+def _direct(case, q, **kw):
+    return _gfx().forward_paged_direct(q.to(dev), case.k_cache, case.v_cache, case.block_table.to(dev),
+                                       torch.from_numpy(case.seq_lens).to(dev), case.scale, **kw)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(48, 8), (8, 4), (6, 1), (8, 2), (16, 4), (64, 8), (32, 32)])
+def test_direct_decode_gqa(Hq, Hkv):
+    lens = [1, 17, 300, 1024, 2500, 16, 33, 4100]
+    case = PagedCase(lens, Hkv, seed=Hq * 10 + Hkv)
+    q = _q((len(lens), Hq, 1, 128), torch.float32, seed=1)
+    out = _direct(case, q)
+    assert_close(to_np(out), case.oracle_bhsd(to_np(q), None), what=f"decode {Hq}/{Hkv}")
+
+
+@pytest.mark.parametrize("v_fmt", ["f16", "bf16", "q8"])
+@pytest.mark.parametrize("qdt", [torch.float32, torch.float16, torch.bfloat16])
+def test_direct_decode_formats(v_fmt, qdt):
+    lens = [5000, 77, 1, 2049]
+    case = PagedCase(lens, 8, v_fmt=v_fmt, seed=3)
+    q = _q((4, 48, 1, 128), qdt, seed=2)
+    out = _direct(case, q)
+    qn, tag = _qnp(q)
+    assert_close(to_np(out), case.oracle_bhsd(qn, tag), what=f"{v_fmt}/{qdt}")
+
+
+@pytest.mark.parametrize("Sq", [2, 4, 5])
+def test_direct_causal_spec_decode(Sq):
+    """Sq query tokens per sequence, causal inside the chunk
+    (q_abs_offset = seq_len - Sq); 6*Sq rows per kv head -> two m-tiles."""
+    lens = [4096, 700, 16, 9000]
+    case = PagedCase(lens, 8, seed=Sq)
+    q = _q((4, 48, Sq, 128), torch.float32, seed=Sq)
+    qa = (case.seq_lens - Sq).astype(np.int32)
+    out = _direct(case, q, q_abs_offset=torch.from_numpy(qa).to(dev))
+    assert_close(to_np(out), case.oracle_bhsd(to_np(q), None, q_abs=qa), what=f"Sq={Sq}")
+
+
+def test_direct_additive_mask():
+    lens = [300, 129]
+    case = PagedCase(lens, 2, seed=9)
+    Sq = 2
+    q = _q((2, 8, Sq, 128), torch.float32, seed=9)
+    g = torch.Generator().manual_seed(5)
+    skv = case.max_blocks * 16
+    mask = torch.where(torch.rand((2, Sq, skv), generator=g) < 0.3, -65504.0, 0.0).half()
+    mask[:, :, 7] = 0.5
+    out = _direct(case, q, mask=mask.to(dev))
+    assert_close(to_np(out), case.oracle_bhsd(to_np(q), None, mask=to_np(mask)), what="mask")
+
+
+def test_empty_and_short_sequences():
+    lens = [0, 1, 15, 16, 17]
+    case = PagedCase(lens, 4, seed=11)
+    q = _q((5, 8, 1, 128), torch.float32, seed=4)
+    o = to_np(_direct(case, q))
+    assert (o[0] == 0).all()
+    assert_close(o, case.oracle_bhsd(to_np(q), None), what="short")
+
+
+def test_config1_decode_token_matches_reference_golden():
+    """BASELINE config 1 decode token (L = 513, Hq/Hkv 8/2, K and V Q8_0)
+    against the reference pipeline's output stored in the golden fixture."""
+    c = np.load(os.path.join(GOLD, "config1_golden.npz"))
+    bt = c["cfg1_block_table"]
+    NB, bs, Hkv, L = 40, 16, 2, 513
+    kc = np.zeros((NB, bs, Hkv, 136), np.uint8)
+    vc = np.zeros_like(kc)
+    for t in range(L):
+        kc[bt[0, t // bs], t % bs] = c["cfg1_k_q8_ref"][t]
+        vc[bt[0, t // bs], t % bs] = c["cfg1_v_q8_ref"][t]
+    q = torch.from_numpy(c["cfg1_q"][512:513]).float().permute(1, 0, 2).unsqueeze(0)   # [1, 8, 1, 128]
+    out = _gfx().forward_paged_direct(q.contiguous().to(dev), torch.from_numpy(kc).to(dev),
+                                      torch.from_numpy(vc).to(dev), torch.from_numpy(bt).to(dev),
+                                      torch.tensor([L], dtype=torch.int32, device=dev), float(c["cfg1_scale"]))
+    ref = c["cfg1_decode_out"].transpose(1, 0, 2)[None]                                 # [1, 8, 1, 128]
+    assert_close(to_np(out), ref, what="config1 decode")
+
+
+def test_paged_attention_varlen_inplace_cache():
+    """vLLM layout: one [NB, 2, bs, Hkv, D] fp16 allocation; the Q8_0 K rows
+    live densely at the start of each page's K half, V stays fp16."""
+    g = _gfx()
+    Hq, Hkv, D, bs = 48, 8, 128, 16
+    lens = [3000, 1, 40, 777]
+    nq = [1, 1, 4, 3]
+    case = PagedCase(lens, Hkv, seed=21)
+    NB = case.NB
+    kv = torch.zeros((NB, 2, bs, Hkv, D), dtype=torch.float16, device=dev)
+    kvb = kv.view(torch.uint8).view(NB, 2, bs * Hkv * 2 * D)
+    rb = case.rb
+    k_view = kvb[:, 0, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
+    k_view.copy_(case.k_cache)
+    kv[:, 1].copy_(case.v_cache)
+    T = sum(nq)
+    q = _q((T, Hq, D), torch.bfloat16, seed=8)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(nq)]), dtype=torch.int32)
+    out = g.paged_attention(q.to(dev), k_view, kv[:, 1], case.block_table.to(dev),
+                            torch.from_numpy(case.seq_lens).to(dev), cu.to(dev), max(nq), max(lens),
+                            case.scale)
+    assert out.dtype == torch.bfloat16
+    ref = case.oracle_varlen(to_np(q), "bf16", nq)
+    assert_close(to_np(out.float()), ref, atol=4e-3, rtol=1.2e-2, what="varlen")
+
+
+def test_config3_decode_full_size_subset_checked():
+    """64 sequences, L ~ U[1K, 32K], GQA 48/8, bf16 Q.
+    The whole batch runs on the GPU; 6 sequences are checked against the
+    oracle (the kernel treats every sequence identically)."""
+    rng = np.random.default_rng(3)
+    lens = rng.integers(1024, 32769, size=64).tolist()
+    case = PagedCase(lens, 8, seed=33)
+    q = _q((64, 48, 1, 128), torch.bfloat16, seed=3)
+    out = to_np(_direct(case, q))
+    pick = [0, 7, int(np.argmax(lens)), int(np.argmin(lens)), 40, 63]
+    ref = case.oracle_bhsd(to_np(q)[pick], "bf16", pick=pick)
+    assert_close(out[pick], ref, what="config3 subset")
+
+
+def test_no_device_error_flagged():
+    assert _gfx().device_error(True) == 0
