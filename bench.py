@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the paged-Q8 attention path on B200.
+
+Metric: paged-Q8 attention -- decode HBM GB/s and prefill
+TFLOP/s at 32K context, GQA 48/8, head_dim 128.
+
+  step (value, the headline line):  one decode batch of BASELINE config 3 --
+      64 sequences, 1 query token each, context lengths ~ U[1K, 32K]
+      (seeded), Hq/Hkv = 48/8, bf16 Q, Q8_0 K + fp16 V paged cache
+      (block_size 16, shuffled pages) built by the store kernel from
+      N(0,1) fp16.  value = algorithmic bytes / time, bytes =
+      sum_s L_s*Hkv*(136 + 256) + Q + O + block table.
+  prefill (extra key): BASELINE config 4 at 32 768 tokens -- one sequence,
+      chunks of 8192 queries against all earlier keys (causal inside the
+      chunk), bf16 Q, same cache format.  FLOPs = 4*D*Hq*sum_chunks
+      [C*s0 + C(C+1)/2].
+
+Multi-GPU (torchrun, one rank per GPU): the kv heads are split across ranks
+as vLLM tensor parallelism does (rank r owns kv heads [r*8/N, (r+1)*8/N) and
+their 6 query heads each); total work is fixed, so scaling is "strong".  No
+collective touches the data path; NCCL is used only for the start barrier
+and the max-over-ranks timing.
+
+`--impl reference` times the CPU restatement of the reference's path
+(oracle/, all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "gfx906-fa-vllm_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "paged-Q8 attn: decode HBM GB/s & prefill TFLOP/s @32K ctx, GQA 48/8 d128"
+HQ, HKV, D, BS = 48, 8, 128, 16
+RB = D // 32 * 34
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        j = json.load(open(p))
+        return float(j["hbm_gbs"]), float(j["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def config3_lens(seed=3):
+    rng = np.random.default_rng(seed)
+    return rng.integers(1024, 32769, size=64).astype(np.int64)
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.rows = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.rows.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 4 + i and r[4 + i] == "Active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# workload construction (on the GPU)
+# ---------------------------------------------------------------------------
+def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
+    """Paged Q8_0 K + fp16 V cache for sequences of `lens` tokens, shuffled
+    pages, filled by the fused store kernel from N(0,1) fp16 K/V."""
+    import torch
+    import gfx906_fa
+    g = torch.Generator(device=device).manual_seed(seed)
+    npg = [(int(L) + BS - 1) // BS for L in lens]
+    NB = sum(npg) + 64
+    perm = torch.randperm(NB, generator=g, device=device).to(torch.int32)
+    MB = max(npg)
+    bt = torch.full((len(lens), MB), -1, dtype=torch.int32, device=device)
+    c = 0
+    for b, n in enumerate(npg):
+        bt[b, :n] = perm[c:c + n]
+        c += n
+    k_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
+    if v_fmt == "q8_0":
+        v_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
+    else:
+        v_cache = torch.zeros((NB, BS, hkv, D), dtype=torch.float16, device=device)
+    chunk = 1 << 16
+    for b, L in enumerate(lens):
+        for t0 in range(0, int(L), chunk):
+            n = min(chunk, int(L) - t0)
+            tpos = torch.arange(t0, t0 + n, device=device)
+            slots = bt[b, tpos // BS].to(torch.int64) * BS + tpos % BS
+            k = torch.randn((n, hkv, D), generator=g, device=device, dtype=torch.float16)
+            v = torch.randn((n, hkv, D), generator=g, device=device, dtype=torch.float16)
+            gfx906_fa.store_kv(k, v, slots, k_cache, v_cache, 2 if v_fmt == "q8_0" else 1)
+    return k_cache, v_cache, bt
+
+
+def decode_bytes(lens, hkv, hq, v_row=256):
+    kv = int(np.sum(lens)) * hkv * (RB + v_row)
+    q = len(lens) * hq * D * 2
+    o = len(lens) * hq * D * 2
+    bt = int(sum((int(L) + BS - 1) // BS for L in lens)) * 4
+    return kv + q + o + bt
+
+
+def prefill_flops(n_tokens, chunk, hq):
+    f = 0
+    for s0 in range(0, n_tokens, chunk):
+        C = min(chunk, n_tokens - s0)
+        f += C * s0 + C * (C + 1) // 2
+    return 4 * D * hq * f
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle restatement, test infrastructure)
+# ---------------------------------------------------------------------------
+def cpu_baseline(seconds_target=10.0, threads=None):
+    """Oracle attention (fp32 dequant + softmax, double accumulation) on the
+    host cores over a bounded sample of config 3: the first sequences until
+    ~seconds_target of work.  Returns GB/s in the decode metric's bytes."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = threads or os.cpu_count()
+    lens = config3_lens()
+    rng = np.random.default_rng(0)
+    done_bytes, elapsed, nseq = 0, 0.0, 0
+    for L in lens:
+        L = int(L)
+        nb = (L + BS - 1) // BS
+        kq = rng.integers(0, 256, size=(nb, BS, HKV, RB), dtype=np.uint8)
+        kq[..., 0::34] = 0x00          # small scales keep the values finite
+        kq[..., 1::34] = 0x20
+        vc = rng.standard_normal((nb, BS, HKV, D)).astype(np.float16)
+        q = rng.standard_normal((1, HQ, D)).astype(np.float32)
+        bt = np.arange(nb, dtype=np.int32).reshape(1, nb)
+        t0 = time.perf_counter()
+        O.attention_paged(q, None, np.array([0]), np.array([1]), kq, vc, bt, np.array([L]), 1 / np.sqrt(D),
+                          HKV, nthreads=threads)
+        elapsed += time.perf_counter() - t0
+        done_bytes += decode_bytes([L], HKV, HQ)
+        nseq += 1
+        if elapsed > seconds_target:
+            break
+    return {"value": done_bytes / elapsed / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{nseq} of the 64 config-3 sequences ({done_bytes / 1e9:.2f} GB of algorithmic bytes), "
+                      f"oracle/q8_oracle.c attention, OpenMP"}, elapsed
+
+
+# ---------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--v-fmt", default="fp16", choices=["fp16", "q8_0"])
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        res, el = cpu_baseline(seconds_target=max(3.0, min(20.0, 2.0 * args.steps)))
+        line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+                "impl": "reference",
+                "config": {"workload": "config3 decode (64 seqs, L~U[1K,32K], GQA 48/8, d128, Q8_0 K)",
+                           "sample": res["sample"]},
+                "cpu_baseline": res,
+                "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import gfx906_fa
+    from gfx906_fa_paged import forward_paged
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    assert HKV % world == 0, "kv heads must split evenly"
+    hkv = HKV // world
+    hq = HQ // world
+
+    # ---------------- decode workload (config 3) ----------------------------
+    lens = config3_lens()
+    B = len(lens)
+    k_cache, v_cache, bt = build_cache(lens, hkv, seed=1000 + rank, device=device, v_fmt=args.v_fmt)
+    sl = torch.tensor(lens, dtype=torch.int32, device=device)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=device)
+    gq = torch.Generator(device=device).manual_seed(7 + rank)
+    q = torch.randn((B, hq, D), generator=gq, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    ones = [1] * B
+    lens_l = [int(x) for x in lens]
+    max_l = int(lens.max())
+    scale = 1.0 / np.sqrt(D)
+
+    def decode_step():
+        gfx906_fa.paged_attention(q, k_cache, v_cache, bt, sl, cu, 1, max_l, scale, out=out,
+                                  query_lens_host=ones, seq_lens_host=lens_l)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+            torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(3, args.warmup)):
+        decode_step()
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    with sampler:
+        barrier()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for i in range(args.steps):
+            ev[i][0].record()
+            decode_step()
+            ev[i][1].record()
+        t_end.record()
+        barrier()
+    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    per_launch_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    v_row = RB if args.v_fmt == "q8_0" else 2 * D
+    bytes_rank = decode_bytes(lens, hkv, hq, v_row)
+    bytes_all = bytes_rank * world
+    ms_per_step = total_ms / args.steps
+    value = bytes_all / (ms_per_step * 1e-3) / 1e9
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    achieved = bytes_rank / (per_launch_ms * 1e-3) / 1e9
+
+    # ---------------- end to end: host buffers through forward_paged --------
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    sl_host = sl.cpu().pin_memory()
+    cu_host = cu.cpu().pin_memory()
+    bt_host = bt.cpu().pin_memory()
+    q_dev = torch.empty_like(q)
+    sl_dev, cu_dev, bt_dev = torch.empty_like(sl), torch.empty_like(cu), torch.empty_like(bt)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        sl_dev.copy_(sl_host, non_blocking=True)
+        cu_dev.copy_(cu_host, non_blocking=True)
+        bt_dev.copy_(bt_host, non_blocking=True)
+        forward_paged(q_dev, None, v_cache, bt_dev, sl_dev, cu_dev, 1, max_l, scale=scale,
+                      key_cache_q8=k_cache, out=out, query_lens_host=ones, seq_lens_host=lens_l)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    h2d = q_host.numel() * 2 + sl_host.numel() * 4 + cu_host.numel() * 4 + bt_host.numel() * 4
+    d2h = out_host.numel() * 2
+    e2e_value = bytes_all / (e2e_ms * 1e-3) / 1e9
+
+    # ---------------- prefill (config 4 at 32K) -----------------------------
+    prefill = None
+    if not args.no_prefill:
+        N, C = 32768, 8192
+        del k_cache, v_cache
+        torch.cuda.empty_cache()
+        kc, vc, btp = build_cache([N], hkv, seed=2000 + rank, device=device)
+        qp = torch.randn((N, hq, D), generator=gq, device=device).to(torch.bfloat16)
+        op = torch.empty_like(qp)
+        chunks = []
+        for s0 in range(0, N, C):
+            n = min(C, N - s0)
+            chunks.append((s0, n, torch.tensor([s0 + n], dtype=torch.int32, device=device),
+                           torch.tensor([0, n], dtype=torch.int32, device=device)))
+
+        def prefill_step():
+            for s0, n, slc, cuc in chunks:
+                gfx906_fa.paged_attention(qp[s0:s0 + n], kc, vc, btp, slc, cuc, n, s0 + n, scale,
+                                          out=op[s0:s0 + n], query_lens_host=[n], seq_lens_host=[s0 + n])
+
+        for _ in range(max(3, args.warmup // 2)):
+            prefill_step()
+        barrier()
+        psteps = max(3, args.steps // 4)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        for _ in range(psteps):
+            prefill_step()
+        p1.record()
+        barrier()
+        pms = max_over_ranks(p0.elapsed_time(p1)) / psteps
+        fl_all = prefill_flops(N, C, HQ)
+        tfs = fl_all / (pms * 1e-3) / 1e12
+        prefill = {"value": tfs, "unit": "TFLOP/s", "ms_per_step": pms,
+                   "workload": "config4 32K: 1 seq x 32768 tokens, 8192-query chunks, causal, GQA 48/8",
+                   "roofline": {"bound": "tensor", "achieved": fl_all / world / (pms * 1e-3) / 1e12,
+                                "peak": tf_peak, "unit": "TFLOP/s",
+                                "frac": fl_all / world / (pms * 1e-3) / 1e12 / tf_peak,
+                                "peak_kind": f"{peak_kind} bf16 burst"},
+                   "gpu_launches_per_step": 3 * len(chunks)}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu, _ = cpu_baseline(seconds_target=10.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16 Q / q8_0 K / "
+            + ("q8_0" if args.v_fmt == "q8_0" else "fp16") + " V, fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": "config3 decode: 64 seqs x 1 query, L~U[1K,32K] seed 3, GQA 48/8, d128, "
+                                   "block 16, shuffled pages",
+                       "kv_heads_per_gpu": hkv, "parallelism": f"kv-head groups x{world}",
+                       "l2": "inputs (%.2f GB per GPU) larger than L2, no flush" % (bytes_rank / 1e9)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None,
+                         "peak_kind": f"{peak_kind} copy bandwidth"},
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "path": "gfx906_fa_paged.forward_paged (reference plugin API), pinned host Q in, O out"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if prefill:
+            line["prefill"] = prefill
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

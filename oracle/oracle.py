@@ -162,14 +162,17 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
                     o_strides: tuple[int, int, int] | None = None,
                     k_strides: tuple[int, int, int] | None = None,
                     v_strides: tuple[int, int, int] | None = None,
-                    nthreads: int = 0) -> np.ndarray:
+                    nthreads: int = 0, bs: int | None = None, v_fmt: str | None = None) -> np.ndarray:
     """fp32 dequant + softmax reference (double accumulation).
 
     Default layouts are vLLM's: q [T, Hq, D] with token rows q_start[b] + t;
     k_cache [NB, bs, Hkv, D/32*34] u8; v_cache [NB, bs, Hkv, D] fp16 (or q8
     bytes when v_q8).  Strides (seq, tok, head) are in elements for q/out and
-    (page, tok, head) in bytes for the caches.
+    (page, tok, head) in bytes for the caches.  bs: tokens per page (default
+    k_cache.shape[1]); v_fmt: "f16" (default), "bf16" or "q8" (= v_q8).
     """
+    vcode = {"f16": 0, "bf16": 1, "q8": 2}[v_fmt or ("q8" if v_q8 else "f16")]
+    v_q8 = vcode == 2
     q = np.ascontiguousarray(q)
     D = q.shape[-1]
     Hq = q.shape[1]                    # [T, Hq, D] or [B, Hq, Sq, D]
@@ -180,7 +183,9 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
         out_shape = q.shape
         o_strides = q_strides
     out = np.zeros(out_shape, dtype=np.float32)
-    NB, bs = k_cache.shape[0], k_cache.shape[1]
+    NB = k_cache.shape[0]
+    if bs is None:
+        bs = k_cache.shape[1]
     rb = row_bytes(D)
     if k_strides is None:
         k_strides = (bs * Hkv * rb, Hkv * rb, rb)
@@ -203,7 +208,7 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
         _i64(q_strides[0]), _i64(q_strides[1]), _i64(q_strides[2]), _p(qs), _p(nq),
         _p(out), _i64(o_strides[0]), _i64(o_strides[1]), _i64(o_strides[2]),
         _p(np.ascontiguousarray(k_cache)), _p(np.ascontiguousarray(v_cache).view(np.uint8)),
-        ctypes.c_int(int(v_q8)), _i64(k_strides[0]), _i64(k_strides[1]), _i64(k_strides[2]),
+        ctypes.c_int(vcode), _i64(k_strides[0]), _i64(k_strides[1]), _i64(k_strides[2]),
         _i64(v_strides[0]), _i64(v_strides[1]), _i64(v_strides[2]), _p(bt), ctypes.c_int(max_blocks),
         ctypes.c_int(bs), _p(kl), _p(qa), _p(mk), _i64(m_seq), _i64(m_tok), ctypes.c_int(B),
         ctypes.c_int(Hq), ctypes.c_int(Hkv), ctypes.c_int(D), ctypes.c_float(scale),
@@ -232,4 +237,4 @@ def attention_bhsd(q: np.ndarray, q_dtype: str | None, k_q8: np.ndarray, v: np.n
         q_strides=(Hq * Sq * D, D, Sq * D), out_shape=(B, Hq, Sq, D),
         o_strides=(Hq * Sq * D, D, Sq * D),
         k_strides=(Hkv * Skv * rb, rb, Skv * rb), v_strides=(Hkv * Skv * vb, vb, Skv * vb),
-        nthreads=nthreads)
+        nthreads=nthreads, bs=max(Skv, 1), v_fmt="q8" if v_q8 else ("bf16" if v.dtype == np.uint16 else "f16"))

@@ -249,7 +249,7 @@ void q8o_dequant_row(const uint8_t* row, int D, float* out) {
 void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_tok_stride,
                    int64_t q_head_stride, const int32_t* q_start, const int32_t* n_q,
                    float* out, int64_t o_seq_stride, int64_t o_tok_stride, int64_t o_head_stride,
-                   const uint8_t* k_cache, const uint8_t* v_cache, int v_q8,
+                   const uint8_t* k_cache, const uint8_t* v_cache, int v_fmt,
                    int64_t k_page_stride, int64_t k_tok_stride, int64_t k_head_stride,
                    int64_t v_page_stride, int64_t v_tok_stride, int64_t v_head_stride,
                    const int32_t* block_table, int max_blocks, int bs, const int32_t* kv_len,
@@ -315,11 +315,12 @@ void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_t
                 l += p;
                 const int phys = block_table[(int64_t)b * max_blocks + k / bs];
                 const uint8_t* vr = v_cache + phys * v_page_stride + (k % bs) * v_tok_stride + h * v_head_stride;
-                if (v_q8) {
+                if (v_fmt == 2) {
                     q8o_dequant_row(vr, D, vrow);
                 } else {
                     const uint16_t* v16 = (const uint16_t*)vr;
-                    for (int d = 0; d < D; ++d) vrow[d] = q8o_f16_to_f32(v16[d]);
+                    for (int d = 0; d < D; ++d)
+                        vrow[d] = v_fmt == 1 ? bf16_to_f32(v16[d]) : q8o_f16_to_f32(v16[d]);
                 }
                 for (int d = 0; d < D; ++d) acc[d] += p * (double)vrow[d];
             }

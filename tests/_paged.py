@@ -73,7 +73,7 @@ class PagedCase:
             q_abs = self.seq_lens - n_q
         return O.attention_paged(q, q_dtype, q_start, n_q, self.k_np, self.v_np,
                                  self.block_table.numpy(), self.seq_lens, self.scale, self.Hkv,
-                                 q_abs=q_abs if causal else None, mask=mask, v_q8=self.v_fmt == "q8",
+                                 q_abs=q_abs if causal else None, mask=mask, v_fmt=self.v_fmt,
                                  v_strides=self._v_strides())
 
     def oracle_bhsd(self, q, q_dtype, q_abs=None, mask=None, pick=None):
@@ -84,7 +84,7 @@ class PagedCase:
         sl = self.seq_lens if pick is None else self.seq_lens[pick]
         return O.attention_paged(q, q_dtype, np.zeros(B, np.int32), np.full(B, Sq, np.int32),
                                  self.k_np, self.v_np, bt, sl, self.scale, self.Hkv, q_abs=q_abs, mask=mask,
-                                 v_q8=self.v_fmt == "q8", q_strides=(Hq * Sq * D, D, Sq * D),
+                                 v_fmt=self.v_fmt, q_strides=(Hq * Sq * D, D, Sq * D),
                                  out_shape=(B, Hq, Sq, D), o_strides=(Hq * Sq * D, D, Sq * D),
                                  v_strides=self._v_strides())
 

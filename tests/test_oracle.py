@@ -115,3 +115,48 @@ def test_f16_conversion_matches_numpy():
         ref = v.astype(np.float16).view(np.uint16)
     got = np.array([O.lib().q8o_f32_to_f16(float(x)) for x in v], dtype=np.uint16)
     assert np.array_equal(got, ref)
+
+
+def _np_attention(q, k, v, scale, kv_len, q_abs=None):
+    """Direct numpy fp64 attention on dense [Hq, Sq, D] / [Hkv, Skv, D]."""
+    Hq, Sq, D = q.shape
+    Hkv = k.shape[0]
+    G = Hq // Hkv
+    out = np.zeros((Hq, Sq, D))
+    for hq in range(Hq):
+        for t in range(Sq):
+            lim = kv_len if q_abs is None else min(kv_len, q_abs + t + 1)
+            if lim <= 0:
+                continue
+            s = k[hq // G, :lim] @ q[hq, t].astype(np.float64) * scale
+            p = np.exp(s - s.max())
+            out[hq, t] = p @ v[hq // G, :lim] / p.sum()
+    return out
+
+
+@pytest.mark.parametrize("v_kind", ["f16", "bf16", "q8"])
+def test_attention_bhsd_matches_direct_numpy(v_kind):
+    """The flat-layout oracle (one page of Skv tokens per sequence) against a
+    plain numpy computation on dequantised tensors."""
+    rng = np.random.default_rng(4)
+    B, Hq, Hkv, Sq, Skv, D = 2, 4, 2, 3, 40, 128
+    q = rng.standard_normal((B, Hq, Sq, D)).astype(np.float32)
+    k16 = rng.standard_normal((B, Hkv, Skv, D)).astype(np.float16)
+    kq = O.quantize_q8_0(k16)
+    v32 = rng.standard_normal((B, Hkv, Skv, D)).astype(np.float32)
+    if v_kind == "q8":
+        v_arr = O.quantize_q8_0(v32.astype(np.float16))
+        v_deq = O.dequantize_q8_0(v_arr, D)
+    elif v_kind == "bf16":
+        v_arr = (v32.view(np.uint32) >> 16).astype(np.uint16)          # truncation to bf16 bits
+        v_deq = (v_arr.astype(np.uint32) << 16).view(np.float32)
+    else:
+        v_arr = v32.astype(np.float16)
+        v_deq = v_arr.astype(np.float32)
+    kv_max = np.array([Skv, 17], np.int32)
+    qa = np.array([Skv - Sq, 5], np.int32)
+    o = O.attention_bhsd(q, None, kq, v_arr, 0.125, kv_max=kv_max, q_abs=qa, v_q8=v_kind == "q8")
+    kd = O.dequantize_q8_0(kq, D)
+    for b in range(B):
+        ref = _np_attention(q[b], kd[b], v_deq[b], 0.125, int(kv_max[b]), int(qa[b]))
+        assert np.abs(o[b] - ref).max() < 1e-5
