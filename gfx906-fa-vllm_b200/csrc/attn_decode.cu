@@ -758,3 +758,55 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
 #undef G9_DEC
   return cudaErrorInvalidValue;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of gfx906_fa_decode_splitk.
+//
+// Some callers cannot allocate device memory at call time -- code running
+// where cudaMalloc is forbidden or unavailable (inside a custom allocator's
+// own callbacks, a runtime that owns every byte of the device heap, or a
+// plugin host with a fixed memory budget).  For them the split-K partial
+// results live in this file-scope device array instead of a caller-provided
+// workspace.  It is g_decode_noalloc_scratch below: kNoAllocScratchBytes
+// (32 MiB), held by every GPU that loads the library until the process
+// exits.  Host code must not use the array's name as a device pointer; the
+// device address is looked up once per device with cudaGetSymbolAddress.
+// ---------------------------------------------------------------------------
+namespace g9 {
+constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;
+static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[kNoAllocScratchBytes];
+}  // namespace g9
+
+#include <mutex>
+
+extern "C" cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch, cudaStream_t stream) {
+  if (!batch) return cudaErrorInvalidValue;
+  // size check before anything touches the device
+  DecodeParams d;
+  int mt;
+  cudaError_t e = plan_decode(*batch, d, mt);
+  if (e != cudaSuccess) return e;
+  const size_t need = d.S_max > 1 ? decode_ws_bytes(d) : 0;
+  if (need > kNoAllocScratchBytes) return cudaErrorInvalidValue;   // batch too large for the static scratch
+  // per-device address of the scratch array, looked up on the first call on
+  // each device (that first call should come before any stream capture)
+  constexpr int kMaxDevices = 64;
+  static void* addr[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+      void* p = nullptr;
+      if ((e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch)) != cudaSuccess) return e;
+      addr[dev] = p;
+    }
+    ptr = addr[dev];
+  }
+  // The decode workspace needs no zeroing: every partial result the combine
+  // step reads is written earlier in the same call.
+  return gfx906_fa_decode_splitk(batch, ptr, kNoAllocScratchBytes, stream);
+}

@@ -169,6 +169,22 @@ size_t gfx906_fa_decode_workspace_size(const G9AttnBatch* batch);
 cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* workspace, size_t workspace_bytes,
                                     cudaStream_t stream);
 
+/* Allocation-free form of gfx906_fa_decode_splitk, for callers that cannot
+ * allocate device memory when they call (code inside an allocator's own
+ * hooks, runtimes that own the whole device heap, plugin hosts with a fixed
+ * budget).  No counterpart in the reference.  The split-K partial results go
+ * to a 32 MiB array that the library holds in static device memory on every
+ * GPU that loads it, until the process exits; batches whose decode workspace
+ * (gfx906_fa_decode_workspace_size) exceeds 32 MiB are rejected with
+ * cudaErrorInvalidValue.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current; make that
+ * first call before any stream capture.  All calls share the one array and
+ * it keeps whatever the last call left; nothing in it needs to start at zero.
+ * Calls that overlap on the GPU (different streams, or different host
+ * threads, on one device) race on it and must be serialised by the caller.
+ * Allocates nothing: no cudaMalloc / cudaFree. */
+cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch, cudaStream_t stream);
+
 /* Tensor-core prefill: for each listed sequence (seq_ids[i], up to nq_cap[i]
  * query tokens, up to kv_cap[i] visible keys -- host-side upper bounds) the
  * visible Q8 pages are dequantised once into fp16 staging tiles in the
