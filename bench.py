@@ -199,6 +199,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--v-fmt", default="fp16", choices=["fp16", "q8_0"])
+    ap.add_argument("--decode-seqs", type=int, default=64,
+                    help="first N sequences of config 3 (profiling uses a smaller case)")
+    ap.add_argument("--prefill-tokens", type=int, default=32768)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -236,7 +240,7 @@ def main():
     hq = HQ // world
 
     # ---------------- decode workload (config 3) ----------------------------
-    lens = config3_lens()
+    lens = config3_lens()[:args.decode_seqs]
     B = len(lens)
     k_cache, v_cache, bt = build_cache(lens, hkv, seed=1000 + rank, device=device, v_fmt=args.v_fmt)
     sl = torch.tensor(lens, dtype=torch.int32, device=device)
@@ -327,7 +331,7 @@ def main():
     # ---------------- prefill (config 4 at 32K) -----------------------------
     prefill = None
     if not args.no_prefill:
-        N, C = 32768, 8192
+        N, C = args.prefill_tokens, 8192
         del k_cache, v_cache
         torch.cuda.empty_cache()
         kc, vc, btp = build_cache([N], hkv, seed=2000 + rank, device=device)
@@ -358,7 +362,7 @@ def main():
         fl_all = prefill_flops(N, C, HQ)
         tfs = fl_all / (pms * 1e-3) / 1e12
         prefill = {"value": tfs, "unit": "TFLOP/s", "ms_per_step": pms,
-                   "workload": "config4 32K: 1 seq x 32768 tokens, 8192-query chunks, causal, GQA 48/8",
+                   "workload": f"config4: 1 seq x {N} tokens, 8192-query chunks, causal, GQA 48/8",
                    "roofline": {"bound": "tensor", "achieved": fl_all / world / (pms * 1e-3) / 1e12,
                                 "peak": tf_peak, "unit": "TFLOP/s",
                                 "frac": fl_all / world / (pms * 1e-3) / 1e12 / tf_peak,
@@ -366,7 +370,7 @@ def main():
                    "gpu_launches_per_step": 3 * len(chunks)}
 
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _ = cpu_baseline(seconds_target=10.0)
 
     if rank == 0:
