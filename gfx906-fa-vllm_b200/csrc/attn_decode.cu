@@ -34,6 +34,7 @@
 // optional fp16 additive mask is added to the scaled score.  Rows without any
 // visible key produce zeros.  Every mbarrier wait is bounded (common.cuh).
 #include <algorithm>
+#include <cstdlib>
 
 #include "attn_common.cuh"
 
@@ -44,7 +45,7 @@ constexpr int D = 128;
 constexpr int PAGE = 16;
 constexpr int NWC = 8;                      // compute warps (warpgroups 0, 1)
 constexpr int NTHREADS = 384;               // + warpgroup 2: warp 8 produces, 9-11 exit
-constexpr int NST = 3;                      // pipeline slots
+constexpr int MAXST = 4;                    // max pipeline slots (3 or 4 chosen per launch)
 constexpr int MAXP = 8;                     // max pages per stage
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*232 + 128*40
@@ -63,13 +64,15 @@ struct DecodeParams {
   int n_items;
   int R_pad;              // 16 * MT
   int rb_k, rb_v;         // bytes of one K / V row
-  int kstride, vstride;   // smem bytes per token row group
-  int k_whole, v_whole;   // 1: one copy per page (else one per token)
+  int kgs, vgs;           // smem bytes per token-pair group (padded to an odd multiple of 16)
+  int kes, ves;           // smem offset of the second token of a pair
+  int pair_k, pair_v;     // 1: one copy per token pair, 0: one copy per token
   int kpage, vpage;       // smem bytes per page
   int stage_bytes;
   int merge_off;          // smem offset of the merge buffer
   int q_off;              // smem offset of the Q tiles (MT == 2)
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
+  int nst;                // pipeline slots of this launch
   float scale_log2;
   float* opart;           // [B][Hkv][S_max][R_pad][D]
   float2* ml;             // [B][Hkv][S_max][R_pad]
@@ -108,7 +111,8 @@ __device__ __forceinline__ void named_sync_compute() {
 }
 
 // MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0).
-template <int MT, int VT, bool MASK>
+// NST: shared-memory pipeline slots.
+template <int MT, int VT, bool MASK, int NST>
 __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodeParams d) {
   using namespace dec;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -130,7 +134,11 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   __syncthreads();
 
   // =========================================================================
-  // producer warpgroup (warp 8 issues copies, 9-11 only give up registers)
+  // producer warpgroup (warp 8 issues copies, 9-11 only give up registers).
+  // Each bulk copy moves the row groups of two consecutive tokens (all HG
+  // heads) into a slot padded to an odd multiple of 16 bytes: half as many
+  // copy requests as one per token, and with the key order below still
+  // conflict-free for the tensor-core operand loads.
   // =========================================================================
   if (warp >= NWC) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
@@ -138,22 +146,25 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     int it = 0;
     bool alive = true;
     const int hgb_k = d.HG * d.rb_k, hgb_v = d.HG * d.rb_v;
-    const int ncopy_k = d.k_whole ? 1 : PAGE;
-    const int ncopy_v = d.v_whole ? 1 : PAGE;
     const uint32_t kbytes_page = (uint32_t)(PAGE * hgb_k);
     const uint32_t vbytes_page = (uint32_t)(PAGE * hgb_v);
-    const int per_page = ncopy_k + ncopy_v;
+    constexpr int kCopies = PAGE;            // 8 K + 8 V two-token copies per page
     for (int item = blockIdx.x; item < d.n_items && alive; item += gridDim.x) {
       int b, z, s, pb, pe, nsplit;
       decode_item(d, item, b, z, s);
       if (!item_pages(d, b, s, pb, pe, nsplit)) continue;
       const int h0 = z * d.HG;
+      // block-table entries are read one stage ahead, so their latency hides
+      // behind the previous stage's copies and the empty-slot wait
+      int phys_next = -1;
+      if (lane < min(d.P, pe - pb)) phys_next = p.block_table[(int64_t)b * p.max_blocks + pb + lane];
       for (int pg = pb;; pg += d.P) {
         const int slot = it % NST;
-        if (it >= NST && !mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) { alive = false; break; }
+        const int phys = phys_next;
         const int npg = max(0, min(d.P, pe - pg));
-        int phys = -1;
-        if (lane < npg) phys = p.block_table[(int64_t)b * p.max_blocks + pg + lane];
+        phys_next = -1;
+        if (lane < min(d.P, pe - pg - d.P)) phys_next = p.block_table[(int64_t)b * p.max_blocks + pg + d.P + lane];
+        if (it >= NST && !mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) { alive = false; break; }
         const bool ok = lane < npg && phys >= 0;
         if (lane < npg && phys < 0) raise_error(ERR_BAD_PAGE);
         if (lane < MAXP) meta[slot].ok[lane] = ok ? 1 : 0;
@@ -171,29 +182,26 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         uint8_t* kdst0 = smem + slot * d.stage_bytes;
         uint8_t* vdst0 = kdst0 + d.P * d.kpage;
         // uniform trip count for the whole warp (the shuffle needs every lane)
-        for (int c0 = 0; c0 < d.P * per_page; c0 += 32) {
+        for (int c0 = 0; c0 < d.P * kCopies; c0 += 32) {
           const int c = c0 + lane;
-          const int j = min(c / per_page, MAXP - 1);
-          const int r = c - j * per_page;
+          const int j = min(c / kCopies, MAXP - 1);
+          const int r = c - j * kCopies;
           const int phys_j = __shfl_sync(0xffffffffu, phys, j);
-          if (c >= d.P * per_page || j >= npg || !((okmask >> j) & 1)) continue;
-          if (r < ncopy_k) {
-            const uint8_t* src = p.k_cache + (int64_t)phys_j * p.k_page_stride + (int64_t)h0 * p.k_head_stride;
-            if (d.k_whole) {
-              bulk_g2s(kdst0 + j * d.kpage, src, PAGE * hgb_k, &full_bar[slot]);
-            } else {
-              bulk_g2s(kdst0 + j * d.kpage + r * d.kstride, src + (int64_t)r * p.k_tok_stride, hgb_k,
-                       &full_bar[slot]);
-            }
-          } else {
-            const int t = r - ncopy_k;
-            const uint8_t* src = p.v_cache + (int64_t)phys_j * p.v_page_stride + (int64_t)h0 * p.v_head_stride;
-            if (d.v_whole) {
-              bulk_g2s(vdst0 + j * d.vpage, src, PAGE * hgb_v, &full_bar[slot]);
-            } else {
-              bulk_g2s(vdst0 + j * d.vpage + t * d.vstride, src + (int64_t)t * p.v_tok_stride, hgb_v,
-                       &full_bar[slot]);
-            }
+          if (c >= d.P * kCopies || j >= npg || !((okmask >> j) & 1)) continue;
+          const int g = r & 7;                   // token pair
+          const bool isk = r < 8;
+          const int pairm = isk ? d.pair_k : d.pair_v;
+          const int hgb = isk ? hgb_k : hgb_v;
+          const uint8_t* src = (isk ? p.k_cache : p.v_cache) +
+                               (int64_t)phys_j * (isk ? p.k_page_stride : p.v_page_stride) +
+                               (int64_t)h0 * (isk ? p.k_head_stride : p.v_head_stride);
+          const int64_t ts = isk ? p.k_tok_stride : p.v_tok_stride;
+          uint8_t* dst = (isk ? kdst0 + j * d.kpage + g * d.kgs : vdst0 + j * d.vpage + g * d.vgs);
+          if (pairm) {
+            bulk_g2s(dst, src + (int64_t)(2 * g) * ts, 2 * hgb, &full_bar[slot]);
+          } else {                               // token rows of the group are not adjacent
+            bulk_g2s(dst, src + (int64_t)(2 * g) * ts, hgb, &full_bar[slot]);
+            bulk_g2s(dst + (isk ? d.kes : d.ves), src + (int64_t)(2 * g + 1) * ts, hgb, &full_bar[slot]);
           }
         }
         ++it;
@@ -415,6 +423,10 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     if (page_ok) {
       const int pg = page0 + sub;
       const int k0 = pg * PAGE;
+      // Key order: accumulator column n of n-tile nt (k-slot nt*8 + n of the
+      // P.V product) is physical key 2n + nt of the page.  Keys 2n and 2n+1
+      // share token-pair group n, so the 8 keys an n-tile (or an 8-row V
+      // matrix) reads lie in 8 different padded groups: no bank conflicts.
       const uint32_t kb = smem_base + slot * d.stage_bytes + sub * d.kpage + hl * d.rb_k;
       const uint32_t vb = smem_base + slot * d.stage_bytes + d.P * d.kpage + sub * d.vpage + hl * d.rb_v;
       // ---------------- S = Q K^T --------------------------------------------
@@ -427,9 +439,9 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           for (int c = 0; c < 4; ++c) sacc[mt][nt][c] = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const uint32_t krow = kb + (nt * 8 + rq) * d.kstride;            // B operand row (key)
-        const uint32_t kcol0 = kb + (nt * 8 + 2 * j4) * d.kstride;       // accumulator column keys
-        const uint32_t kcol1 = kcol0 + d.kstride;
+        const uint32_t krow = kb + rq * d.kgs + nt * d.kes;              // B operand row: key 2*rq + nt
+        const uint32_t kcol0 = kb + (2 * j4) * d.kgs + nt * d.kes;       // accumulator column keys
+        const uint32_t kcol1 = kcol0 + d.kgs;
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t qb = krow + blk * QBLOCK + 2 + 2 * j4;
@@ -456,9 +468,12 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         }
       }
       // ---------------- mask + online softmax (base 2) ------------------------
+      // pages every row sees completely need no per-element mask
+      const bool page_full = !MASK && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1);
       uint32_t pa[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
+        float alpha2[2];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int r = mt * 16 + rq + hh * 8;
@@ -471,14 +486,16 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-              const int k = k0 + nt * 8 + 2 * j4 + c;
               float x = sacc[mt][nt][hh * 2 + c] * d.scale_log2;
-              if constexpr (MASK) {
-                if (r < cR && k < ckv)
-                  x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
-                      (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+              if (!page_full) {
+                const int k = k0 + 4 * j4 + 2 * c + nt;            // physical key of this column
+                if constexpr (MASK) {
+                  if (r < cR && k < ckv)
+                    x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                        (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+                }
+                x = k < kv_lim ? x : -INFINITY;
               }
-              x = k < kv_lim ? x : -INFINITY;
               sacc[mt][nt][hh * 2 + c] = x;
               mx = fmaxf(mx, x);
             }
@@ -487,6 +504,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           const float mn = fmaxf(mrow[mt][hh], mx);
           const float mu = mn == -INFINITY ? 0.f : mn;
           const float alpha = fast_exp2(mrow[mt][hh] - mu);
+          alpha2[hh] = alpha;
           mrow[mt][hh] = mn;
           float ls = 0.f;
 #pragma unroll
@@ -498,10 +516,16 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
               ls += pv;
             }
           lrow[mt][hh] = lrow[mt][hh] * alpha + ls;
+        }
+        // the running max rarely grows after the first pages: skip the O
+        // rescale when no row of the warp changed
+        if (__any_sync(0xffffffffu, alpha2[0] != 1.f || alpha2[1] != 1.f)) {
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt) {
-            o[mt][nt][hh * 2] *= alpha;
-            o[mt][nt][hh * 2 + 1] *= alpha;
+            o[mt][nt][0] *= alpha2[0];
+            o[mt][nt][1] *= alpha2[0];
+            o[mt][nt][2] *= alpha2[1];
+            o[mt][nt][3] *= alpha2[1];
           }
         }
         if constexpr (VT == 1) {
@@ -521,7 +545,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         // ldmatrix.trans: thread i addresses matrix i/8 row i%8; matrices
         // (keys 0-7 | 8-15) x (d block nt | nt+1)
         const int mi = lane >> 3, ri = lane & 7;
-        const uint32_t vrow = vb + ((mi & 1) * 8 + ri) * d.vstride + (mi >> 1) * 16;
+        const uint32_t vrow = vb + ri * d.vgs + (mi & 1) * d.ves + (mi >> 1) * 16;
 #pragma unroll
         for (int ntp = 0; ntp < 8; ++ntp) {
           uint32_t r4[4];
@@ -541,10 +565,11 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         }
       } else {
         // V rows are Q8_0: B fragment element (key k, dim n) = q8[k][n] * d[k][n/32]
-        const uint32_t r0 = vb + (2 * j4) * d.vstride;       // keys 2j, 2j+1, 2j+8, 2j+9
-        const uint32_t r1 = r0 + d.vstride;
-        const uint32_t r8 = r0 + 8 * d.vstride;
-        const uint32_t r9 = r8 + d.vstride;
+        // k-slots 2j, 2j+1, 2j+8, 2j+9 = keys 4j, 4j+2, 4j+1, 4j+3
+        const uint32_t r0 = vb + (2 * j4) * d.vgs;
+        const uint32_t r1 = r0 + d.vgs;
+        const uint32_t r8 = r0 + d.ves;
+        const uint32_t r9 = r1 + d.ves;
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t so = blk * QBLOCK;
@@ -655,30 +680,42 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // dense pages: the rows of one token (all heads) are contiguous
   if (p.k_head_stride != d.rb_k || p.k_tok_stride != (int64_t)Hkv * d.rb_k) return cudaErrorInvalidValue;
   if (p.v_head_stride != d.rb_v || p.v_tok_stride != (int64_t)Hkv * d.rb_v) return cudaErrorInvalidValue;
-  if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.v_page_stride) & 15)
-    return cudaErrorInvalidValue;
-  auto plan_rows = [&](int rb, int64_t tok_stride, int& whole, int& stride, int& page) -> bool {
+  // Two-token copies when the row groups of consecutive tokens are adjacent
+  // (all kv heads in one CTA), else one copy per token; either way a pair
+  // group is padded to an odd multiple of 16 bytes.  Copies need 16-byte
+  // aligned sources and sizes.
+  auto plan_rows = [&](int rb, int64_t tok_stride, int64_t head_stride, int64_t page_stride, int& pairm, int& gs,
+                       int& es, int& page) -> bool {
     const int grp = d.HG * rb;
-    if (grp % 16 == 0 && tok_stride % 16 == 0) {     // one copy per token row group
-      whole = 0;
-      stride = pad_odd16(grp);
-      page = PAGE * stride;
-      return true;
+    if (page_stride % 16 || ((int64_t)d.HG * head_stride) % 16) return false;
+    if (tok_stride == grp && (2 * grp) % 16 == 0) {
+      pairm = 1;
+      gs = pad_odd16(2 * grp);
+      es = grp;
+    } else {
+      if (grp % 16 || tok_stride % 16) return false;
+      pairm = 0;
+      const int one = pad_odd16(grp);
+      gs = 2 * one;                              // keys 2n, 2n+1 at n*gs, n*gs + one
+      es = one;
+      if (((gs / 16) & 1) == 0) gs += 16;        // keep the pair stride odd in 16-byte units
     }
-    if (d.HG == Hkv && (PAGE * grp) % 16 == 0) {     // one copy of the whole page
-      whole = 1;
-      stride = grp;
-      page = PAGE * grp;
-      return true;
-    }
-    return false;
+    page = (PAGE / 2) * gs;
+    return true;
   };
-  if (!plan_rows(d.rb_k, p.k_tok_stride, d.k_whole, d.kstride, d.kpage)) return cudaErrorInvalidValue;
-  if (!plan_rows(d.rb_v, p.v_tok_stride, d.v_whole, d.vstride, d.vpage)) return cudaErrorInvalidValue;
+  if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache) & 15) return cudaErrorInvalidValue;
+  if (!plan_rows(d.rb_k, p.k_tok_stride, p.k_head_stride, p.k_page_stride, d.pair_k, d.kgs, d.kes, d.kpage))
+    return cudaErrorInvalidValue;
+  if (!plan_rows(d.rb_v, p.v_tok_stride, p.v_head_stride, p.v_page_stride, d.pair_v, d.vgs, d.ves, d.vpage))
+    return cudaErrorInvalidValue;
   d.stage_bytes = d.P * (d.kpage + d.vpage);
-  d.merge_off = NST * d.stage_bytes;
   const int wph = NWC / d.HG;
   const int merge_bytes = wph > 1 ? d.HG * mt * (16 * 4 + 4) * 32 * 4 : 0;
+  const int q_bytes = mt == 2 ? d.HG * mt * 16 * QROW : 0;
+  // 4 slots when they fit in shared memory (227 KB per CTA), else 3
+  d.nst = MAXST;
+  if ((int64_t)d.nst * d.stage_bytes + merge_bytes + q_bytes > 227 * 1024) d.nst = 3;
+  d.merge_off = d.nst * d.stage_bytes;
   d.q_off = d.merge_off + merge_bytes;
   d.scale_log2 = p.scale * kLog2e;
   // chunking: enough chunks to keep every SM busy several times over
@@ -703,7 +740,7 @@ static size_t decode_ws_bytes(const DecodeParams& d) {
 template <int MT, int VT, bool MASK>
 static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)d.HG * MT * 16 * dec::QROW : 0);
-  auto kern = decode_kernel<MT, VT, MASK>;
+  auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4> : decode_kernel<MT, VT, MASK, 3>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::max(1, std::min(d.n_items, num_sms()));
