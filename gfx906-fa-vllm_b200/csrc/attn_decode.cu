@@ -64,9 +64,8 @@ struct DecodeParams {
   int n_items;
   int R_pad;              // 16 * MT
   int rb_k, rb_v;         // bytes of one K / V row
-  int kgs, vgs;           // smem bytes per token-pair group (padded to an odd multiple of 16)
-  int kes, ves;           // smem offset of the second token of a pair
-  int pair_k, pair_v;     // 1: one copy per token pair, 0: one copy per token
+  int kgs, vgs;           // smem bytes per K group (4 tokens) / V group (2 tokens), padded to odd x 16
+  int contig;             // 1: rows of consecutive tokens are adjacent (one copy per group)
   int kpage, vpage;       // smem bytes per page
   int stage_bytes;
   int merge_off;          // smem offset of the merge buffer
@@ -148,7 +147,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     const int hgb_k = d.HG * d.rb_k, hgb_v = d.HG * d.rb_v;
     const uint32_t kbytes_page = (uint32_t)(PAGE * hgb_k);
     const uint32_t vbytes_page = (uint32_t)(PAGE * hgb_v);
-    constexpr int kCopies = PAGE;            // 8 K + 8 V two-token copies per page
+    constexpr int kCopies = 2 * PAGE;        // copy slots per page (12 used with adjacent rows, 32 without)
     for (int item = blockIdx.x; item < d.n_items && alive; item += gridDim.x) {
       int b, z, s, pb, pe, nsplit;
       decode_item(d, item, b, z, s);
@@ -188,20 +187,24 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           const int r = c - j * kCopies;
           const int phys_j = __shfl_sync(0xffffffffu, phys, j);
           if (c >= d.P * kCopies || j >= npg || !((okmask >> j) & 1)) continue;
-          const int g = r & 7;                   // token pair
-          const bool isk = r < 8;
-          const int pairm = isk ? d.pair_k : d.pair_v;
+          // K: 4 groups of 4 tokens, V: 8 groups of 2 tokens (slots 0-3 / 4-11
+          // as whole-group copies, or 0-15 / 16-31 token by token)
+          const int nkc = d.contig ? 4 : 16;
+          const bool isk = r < nkc;
+          const int q = isk ? r : r - nkc;
+          if (!isk && q >= (d.contig ? 8 : 16)) continue;
           const int hgb = isk ? hgb_k : hgb_v;
+          const int gt = isk ? 4 : 2;             // tokens per group
           const uint8_t* src = (isk ? p.k_cache : p.v_cache) +
                                (int64_t)phys_j * (isk ? p.k_page_stride : p.v_page_stride) +
                                (int64_t)h0 * (isk ? p.k_head_stride : p.v_head_stride);
           const int64_t ts = isk ? p.k_tok_stride : p.v_tok_stride;
-          uint8_t* dst = (isk ? kdst0 + j * d.kpage + g * d.kgs : vdst0 + j * d.vpage + g * d.vgs);
-          if (pairm) {
-            bulk_g2s(dst, src + (int64_t)(2 * g) * ts, 2 * hgb, &full_bar[slot]);
-          } else {                               // token rows of the group are not adjacent
-            bulk_g2s(dst, src + (int64_t)(2 * g) * ts, hgb, &full_bar[slot]);
-            bulk_g2s(dst + (isk ? d.kes : d.ves), src + (int64_t)(2 * g + 1) * ts, hgb, &full_bar[slot]);
+          uint8_t* base = isk ? kdst0 + j * d.kpage : vdst0 + j * d.vpage;
+          const int gs = isk ? d.kgs : d.vgs;
+          if (d.contig) {
+            bulk_g2s(base + q * gs, src + (int64_t)(gt * q) * ts, gt * hgb, &full_bar[slot]);
+          } else {                                // token rows of a group are not adjacent in HBM
+            bulk_g2s(base + (q / gt) * gs + (q % gt) * hgb, src + (int64_t)q * ts, hgb, &full_bar[slot]);
           }
         }
         ++it;
@@ -424,9 +427,15 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
       const int pg = page0 + sub;
       const int k0 = pg * PAGE;
       // Key order: accumulator column n of n-tile nt (k-slot nt*8 + n of the
-      // P.V product) is physical key 2n + nt of the page.  Keys 2n and 2n+1
-      // share token-pair group n, so the 8 keys an n-tile (or an 8-row V
-      // matrix) reads lie in 8 different padded groups: no bank conflicts.
+      // P.V product) is physical key 4*(n/2) + e, e = {0,3} for nt = 0 and
+      // {1,2} for nt = 1 (by n & 1).  An n-tile then takes one key of each
+      // V pair group and, per 4-token K group, two keys whose rows sit in
+      // different bank halves -- the 8 rows it reads are conflict-free for
+      // both the K fragments and the ldmatrix V fragments.
+      const int hgb_k = d.HG * d.rb_k, hgb_v = d.HG * d.rb_v;
+      auto kaddr = [&](int key) { return (uint32_t)((key >> 2) * d.kgs + (key & 3) * hgb_k); };
+      auto vaddr = [&](int key) { return (uint32_t)((key >> 1) * d.vgs + (key & 1) * hgb_v); };
+      auto slot_key = [](int nt, int n) { return 4 * (n >> 1) + (nt == 0 ? 3 * (n & 1) : 1 + (n & 1)); };
       const uint32_t kb = smem_base + slot * d.stage_bytes + sub * d.kpage + hl * d.rb_k;
       const uint32_t vb = smem_base + slot * d.stage_bytes + d.P * d.kpage + sub * d.vpage + hl * d.rb_v;
       // ---------------- S = Q K^T --------------------------------------------
@@ -439,9 +448,9 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           for (int c = 0; c < 4; ++c) sacc[mt][nt][c] = 0.f;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const uint32_t krow = kb + rq * d.kgs + nt * d.kes;              // B operand row: key 2*rq + nt
-        const uint32_t kcol0 = kb + (2 * j4) * d.kgs + nt * d.kes;       // accumulator column keys
-        const uint32_t kcol1 = kcol0 + d.kgs;
+        const uint32_t krow = kb + kaddr(slot_key(nt, rq));              // B operand row (key)
+        const uint32_t kcol0 = kb + kaddr(slot_key(nt, 2 * j4));         // accumulator column keys
+        const uint32_t kcol1 = kb + kaddr(slot_key(nt, 2 * j4 + 1));
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t qb = krow + blk * QBLOCK + 2 + 2 * j4;
@@ -488,7 +497,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             for (int c = 0; c < 2; ++c) {
               float x = sacc[mt][nt][hh * 2 + c] * d.scale_log2;
               if (!page_full) {
-                const int k = k0 + 4 * j4 + 2 * c + nt;            // physical key of this column
+                const int k = k0 + 4 * j4 + (nt == 0 ? 3 * c : 1 + c);   // physical key of column 2*j4 + c
                 if constexpr (MASK) {
                   if (r < cR && k < ckv)
                     x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
@@ -545,7 +554,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         // ldmatrix.trans: thread i addresses matrix i/8 row i%8; matrices
         // (keys 0-7 | 8-15) x (d block nt | nt+1)
         const int mi = lane >> 3, ri = lane & 7;
-        const uint32_t vrow = vb + ri * d.vgs + (mi & 1) * d.ves + (mi >> 1) * 16;
+        const uint32_t vrow = vb + vaddr(slot_key(mi & 1, ri)) + (mi >> 1) * 16;
 #pragma unroll
         for (int ntp = 0; ntp < 8; ++ntp) {
           uint32_t r4[4];
@@ -565,11 +574,11 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         }
       } else {
         // V rows are Q8_0: B fragment element (key k, dim n) = q8[k][n] * d[k][n/32]
-        // k-slots 2j, 2j+1, 2j+8, 2j+9 = keys 4j, 4j+2, 4j+1, 4j+3
-        const uint32_t r0 = vb + (2 * j4) * d.vgs;
-        const uint32_t r1 = r0 + d.vgs;
-        const uint32_t r8 = r0 + d.ves;
-        const uint32_t r9 = r1 + d.ves;
+        // k-slots 2j, 2j+1, 2j+8, 2j+9
+        const uint32_t r0 = vb + vaddr(slot_key(0, 2 * j4));
+        const uint32_t r1 = vb + vaddr(slot_key(0, 2 * j4 + 1));
+        const uint32_t r8 = vb + vaddr(slot_key(1, 2 * j4));
+        const uint32_t r9 = vb + vaddr(slot_key(1, 2 * j4 + 1));
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t so = blk * QBLOCK;
@@ -680,34 +689,25 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // dense pages: the rows of one token (all heads) are contiguous
   if (p.k_head_stride != d.rb_k || p.k_tok_stride != (int64_t)Hkv * d.rb_k) return cudaErrorInvalidValue;
   if (p.v_head_stride != d.rb_v || p.v_tok_stride != (int64_t)Hkv * d.rb_v) return cudaErrorInvalidValue;
-  // Two-token copies when the row groups of consecutive tokens are adjacent
-  // (all kv heads in one CTA), else one copy per token; either way a pair
-  // group is padded to an odd multiple of 16 bytes.  Copies need 16-byte
-  // aligned sources and sizes.
-  auto plan_rows = [&](int rb, int64_t tok_stride, int64_t head_stride, int64_t page_stride, int& pairm, int& gs,
-                       int& es, int& page) -> bool {
-    const int grp = d.HG * rb;
-    if (page_stride % 16 || ((int64_t)d.HG * head_stride) % 16) return false;
-    if (tok_stride == grp && (2 * grp) % 16 == 0) {
-      pairm = 1;
-      gs = pad_odd16(2 * grp);
-      es = grp;
-    } else {
-      if (grp % 16 || tok_stride % 16) return false;
-      pairm = 0;
-      const int one = pad_odd16(grp);
-      gs = 2 * one;                              // keys 2n, 2n+1 at n*gs, n*gs + one
-      es = one;
-      if (((gs / 16) & 1) == 0) gs += 16;        // keep the pair stride odd in 16-byte units
-    }
-    page = (PAGE / 2) * gs;
-    return true;
-  };
-  if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache) & 15) return cudaErrorInvalidValue;
-  if (!plan_rows(d.rb_k, p.k_tok_stride, p.k_head_stride, p.k_page_stride, d.pair_k, d.kgs, d.kes, d.kpage))
+  // Shared-memory layout per page: K in 4 groups of 4 tokens, V in 8 groups of
+  // 2 tokens, each group padded to an odd multiple of 16 bytes.  When the
+  // row groups of consecutive tokens are adjacent in HBM (all kv heads in one
+  // CTA) a group is one bulk copy, else one copy per token.  Copies need
+  // 16-byte aligned sources and sizes.
+  const int hgk = d.HG * d.rb_k, hgv = d.HG * d.rb_v;
+  d.contig = p.k_tok_stride == hgk && p.v_tok_stride == hgv;
+  if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.v_page_stride) & 15)
     return cudaErrorInvalidValue;
-  if (!plan_rows(d.rb_v, p.v_tok_stride, p.v_head_stride, p.v_page_stride, d.pair_v, d.vgs, d.ves, d.vpage))
-    return cudaErrorInvalidValue;
+  if (((int64_t)d.HG * p.k_head_stride) % 16 || ((int64_t)d.HG * p.v_head_stride) % 16) return cudaErrorInvalidValue;
+  if (d.contig) {
+    if ((2 * hgk) % 16 || (2 * hgv) % 16) return cudaErrorInvalidValue;
+  } else {
+    if (hgk % 16 || hgv % 16 || p.k_tok_stride % 16 || p.v_tok_stride % 16) return cudaErrorInvalidValue;
+  }
+  d.kgs = pad_odd16(4 * hgk);
+  d.vgs = pad_odd16(2 * hgv);
+  d.kpage = (PAGE / 4) * d.kgs;
+  d.vpage = (PAGE / 2) * d.vgs;
   d.stage_bytes = d.P * (d.kpage + d.vpage);
   const int wph = NWC / d.HG;
   const int merge_bytes = wph > 1 ? d.HG * mt * (16 * 4 + 4) * 32 * 4 : 0;
