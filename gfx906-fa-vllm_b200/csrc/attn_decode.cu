@@ -73,6 +73,7 @@ struct DecodeParams {
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
   int nst;                // pipeline slots of this launch
   float scale_log2;
+  unsigned int* counter;  // work-queue counter (zeroed before the launch)
   float* opart;           // [B][Hkv][S_max][R_pad][D]
   float2* ml;             // [B][Hkv][S_max][R_pad]
 };
@@ -148,7 +149,12 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     const uint32_t kbytes_page = (uint32_t)(PAGE * hgb_k);
     const uint32_t vbytes_page = (uint32_t)(PAGE * hgb_v);
     constexpr int kCopies = 2 * PAGE;        // copy slots per page (12 used with adjacent rows, 32 without)
-    for (int item = blockIdx.x; item < d.n_items && alive; item += gridDim.x) {
+    // items are claimed dynamically, so CTAs that drew short chunks take more
+    while (alive) {
+      int item = 0;
+      if (lane == 0) item = (int)atomicAdd(d.counter, 1u);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item >= d.n_items) break;
       int b, z, s, pb, pe, nsplit;
       decode_item(d, item, b, z, s);
       if (!item_pages(d, b, s, pb, pe, nsplit)) continue;
@@ -275,26 +281,47 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
       }
       named_sync_compute();
     } else {
+      // all loads of both rows are issued before any conversion, so the
+      // item switch costs one memory latency instead of one per element
+      const int rA = rq, rB = rq + 8;
+      const bool vA = rA < cR, vB = rB < cR;
+      const int tA = vA ? rA / d.G : 0, tB = vB ? rB / d.G : 0;
+      const int64_t baseA = vA ? q_offset(p, b, tA, h * d.G + (rA - tA * d.G)) : 0;
+      const int64_t baseB = vB ? q_offset(p, b, tB, h * d.G + (rB - tB * d.G)) : 0;
+      if (p.q_dtype == DT_F32) {
+        float2 xa[16], xb[16];
+        const float* qf = reinterpret_cast<const float*>(p.q);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int r = rq + half * 8;
-        const bool valid = r < cR;
-        const int t = valid ? r / d.G : 0;
-        const int hq = h * d.G + (valid ? r - t * d.G : 0);
-        const int64_t base = valid ? q_offset(p, b, t, hq) : 0;
+        for (int i = 0; i < 16; ++i) {
+          const int dd = (i >> 1) * 16 + (i & 1) * 8 + 2 * j4;
+          xa[i] = vA ? *reinterpret_cast<const float2*>(qf + baseA + dd) : make_float2(0.f, 0.f);
+          xb[i] = vB ? *reinterpret_cast<const float2*>(qf + baseB + dd) : make_float2(0.f, 0.f);
+        }
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
+        for (int i = 0; i < 16; ++i) {
+          // a0: (row, k lo)  a1: (row+8, k lo)  a2: (row, k hi)  a3: (row+8, k hi)
+          qa[0][i >> 1][(i & 1) * 2 + 0] = pack_half2(xa[i].x, xa[i].y);
+          qa[0][i >> 1][(i & 1) * 2 + 1] = pack_half2(xb[i].x, xb[i].y);
+        }
+      } else {
+        uint32_t xa[16], xb[16];
+        const uint16_t* qh = reinterpret_cast<const uint16_t*>(p.q);
 #pragma unroll
-          for (int hi = 0; hi < 2; ++hi) {
-            const int dd = ks * 16 + hi * 8 + 2 * j4;
-            float x0 = 0.f, x1 = 0.f;
-            if (valid) {
-              x0 = load_one(p.q, base + dd, p.q_dtype);
-              x1 = load_one(p.q, base + dd + 1, p.q_dtype);
-            }
-            // a0: (row, k lo)  a1: (row+8, k lo)  a2: (row, k hi)  a3: (row+8, k hi)
-            qa[0][ks][hi * 2 + half] = pack_half2(x0, x1);
+        for (int i = 0; i < 16; ++i) {
+          const int dd = (i >> 1) * 16 + (i & 1) * 8 + 2 * j4;
+          xa[i] = vA ? *reinterpret_cast<const uint32_t*>(qh + baseA + dd) : 0u;
+          xb[i] = vB ? *reinterpret_cast<const uint32_t*>(qh + baseB + dd) : 0u;
+        }
+        const bool bf = p.q_dtype == DT_BF16;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          uint32_t a = xa[i], c = xb[i];
+          if (bf) {
+            a = pack_half2(__uint_as_float(a << 16), __uint_as_float(a & 0xffff0000u));
+            c = pack_half2(__uint_as_float(c << 16), __uint_as_float(c & 0xffff0000u));
           }
+          qa[0][i >> 1][(i & 1) * 2 + 0] = a;
+          qa[0][i >> 1][(i & 1) * 2 + 1] = c;
         }
       }
     }
@@ -734,7 +761,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
 static size_t decode_ws_bytes(const DecodeParams& d) {
   const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
   const size_t o = rows * dec::D * sizeof(float);
-  return ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
+  return 256 + ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
 }
 
 template <int MT, int VT, bool MASK>
@@ -776,13 +803,16 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
   cudaError_t e = plan_decode(*batch, d, mt);
   if (e != cudaSuccess) return e;
   if (batch->num_seqs == 0 || batch->seq_q == 0) return cudaSuccess;
-  if (d.S_max > 1) {
-    if (!workspace || workspace_bytes < decode_ws_bytes(d) || ((uintptr_t)workspace & 15))
-      return cudaErrorInvalidValue;
+  if (!workspace || workspace_bytes < decode_ws_bytes(d) || ((uintptr_t)workspace & 15)) return cudaErrorInvalidValue;
+  {
+    // [0, 256): work-queue counter; then partial O and (max, sum) rows
     const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
-    d.opart = reinterpret_cast<float*>(workspace);
-    d.ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(workspace) +
-                                     (((rows * dec::D * sizeof(float)) + 255) & ~(size_t)255));
+    uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
+    d.counter = reinterpret_cast<unsigned int*>(w);
+    d.opart = reinterpret_cast<float*>(w + 256);
+    d.ml = reinterpret_cast<float2*>(w + 256 + (((rows * dec::D * sizeof(float)) + 255) & ~(size_t)255));
+    cudaError_t ze = cudaMemsetAsync(d.counter, 0, sizeof(unsigned int), stream);
+    if (ze != cudaSuccess) return ze;
   }
   const int vt = batch->v_fmt;
   const bool mask = batch->mask != nullptr;
@@ -823,7 +853,7 @@ extern "C" cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch,
   int mt;
   cudaError_t e = plan_decode(*batch, d, mt);
   if (e != cudaSuccess) return e;
-  const size_t need = d.S_max > 1 ? decode_ws_bytes(d) : 0;
+  const size_t need = decode_ws_bytes(d);
   if (need > kNoAllocScratchBytes) return cudaErrorInvalidValue;   // batch too large for the static scratch
   // per-device address of the scratch array, looked up on the first call on
   // each device (that first call should come before any stream capture)
@@ -843,7 +873,9 @@ extern "C" cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch,
     }
     ptr = addr[dev];
   }
-  // The decode workspace needs no zeroing: every partial result the combine
-  // step reads is written earlier in the same call.
+  // Nothing in the array has to be cleared by the caller: the work-queue
+  // counter at its start is zeroed by the call itself (cudaMemsetAsync on the
+  // stream), and every partial result the combine step reads is written
+  // earlier in the same call.
   return gfx906_fa_decode_splitk(batch, ptr, kNoAllocScratchBytes, stream);
 }

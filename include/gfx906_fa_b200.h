@@ -179,7 +179,8 @@ cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* workspace, s
  * cudaErrorInvalidValue.  The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress) with that device current; make that
  * first call before any stream capture.  All calls share the one array and
- * it keeps whatever the last call left; nothing in it needs to start at zero.
+ * it keeps whatever the last call left; the one part that must start at zero
+ * (a work counter) is cleared by each call on its stream.
  * Calls that overlap on the GPU (different streams, or different host
  * threads, on one device) race on it and must be serialised by the caller.
  * Allocates nothing: no cudaMalloc / cudaFree. */
