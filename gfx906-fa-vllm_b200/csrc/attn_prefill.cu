@@ -10,7 +10,7 @@
 //
 //  1. pack (CUDA cores, HBM-bound): the Q8_0 pages a prefill sequence can
 //     see are dequantised ONCE per call into fp16 staging tiles -- K as
-//     [key][d] rows, V transposed as [d][key] 128x128 tiles -- and Q is
+//     [key][d] rows, V transposed as [d][key] 144x128 tiles (V^T, ones, zeros) -- and Q is
 //     converted to fp16 with the GQA group packed into rows (row = t*G + g).
 //     Dequantisation is one rounding: q8 * d computed in fp32, rounded to
 //     fp16.  Doing it once per call instead of once per (query tile, kv
@@ -21,13 +21,16 @@
 //     warp 0 drives TMA (128-byte swizzled tiles), warp 1 allocates tensor
 //     memory and issues tcgen05.mma from one thread, warps 4-7 run the
 //     softmax with one thread per query row (row i = TMEM lane i).  Tensor
-//     memory: S double-buffered (2 x 128 fp32 columns), O (128 columns), P
-//     double-buffered as packed fp16 (2 x 64 columns).  S = Q K^T reads both
-//     operands from shared memory; O += P V reads P from tensor memory and
-//     V^T from shared memory.  The MMA order S0 S1 PV0 S2 PV1 ... lets the
-//     next S tile run while the softmax works on the current one.  The
-//     running max is rescaled lazily (only when it grows by more than 2^8),
-//     so O in tensor memory is rarely touched by the softmax warps.
+//     memory: S double-buffered (2 x 128 fp32 columns); P_j is written as
+//     packed fp16 over the first 64 columns of S_j; O has 144 columns.
+//     S = Q K^T reads both operands from shared memory; O += P V reads P
+//     from tensor memory and V^T from shared memory.  Each V^T tile carries
+//     a row of ones after its 128 dims, so column 128 of O accumulates the
+//     softmax row sums on the tensor core from the same fp16 P.  The MMA
+//     order S0 S1 PV0 S2 PV1 ... lets the next S tile run while the softmax
+//     works on the current one.  Exponentials are taken on fp16 pairs
+//     (ex2.approx.f16x2).  The running max is rescaled lazily (only when it
+//     grows by more than 2^8), so O is rarely touched by the softmax warps.
 //
 // Masking is the reference's: keys k >= kv_len ignored; causal rule
 // k <= q_abs[b] + t (fattn-q8.cuh:646-654); optional fp16 additive mask.
@@ -47,7 +50,9 @@ constexpr int BM = 128;          // query rows per CTA
 constexpr int BN = 128;          // keys per tile
 constexpr int KST = 3;           // K smem stages
 constexpr int VST = 2;           // V smem stages
-constexpr int TILE_BYTES = BM * D * 2;   // 32 KB
+constexpr int TILE_BYTES = BM * D * 2;   // 32 KB (Q and K tiles)
+constexpr int VROWS = D + 16;            // V^T tile rows: 128 dims + a row of ones + 15 zero rows
+constexpr int VTILE_BYTES = VROWS * BN * 2;   // 36 KB
 constexpr int MAXS = 128;        // prefill sequences per launch
 constexpr int NTHREADS = 256;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -68,7 +73,7 @@ struct PrefillParams {
   float scale_log2;
   __half* qp;                    // [Hkv][RT*128][128]
   __half* kp;                    // [Hkv][KT*128][128]
-  __half* vt;                    // [Hkv][KT][128 d][128 keys]
+  __half* vt;                    // [Hkv][KT][144][128 keys]: V^T, then ones, then zeros
 };
 
 __device__ __forceinline__ int find_seq(const int* off, int n, int x) {
@@ -152,13 +157,16 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
   }
   __syncthreads();
   // transposed write: V^T tile [d][key], 8 keys (16 bytes) per item
-  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)D * BN;
-  for (int it = threadIdx.x; it < D * (BN / 8); it += blockDim.x) {
+  // rows 0..127: V^T; row 128: ones, so that the P.V product also yields the
+  // softmax row sums in fp32; rows 129..143: zeros (N must be a multiple of 16)
+  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)VROWS * BN;
+  for (int it = threadIdx.x; it < VROWS * (BN / 8); it += blockDim.x) {
     const int d = it / (BN / 8);
     const int k8 = (it % (BN / 8)) * 8;
     __align__(16) __half t8[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) t8[e] = vs[k8 + e][d];
+    for (int e = 0; e < 8; ++e)
+      t8[e] = d < D ? vs[k8 + e][d] : __float2half_rn(d == D ? 1.f : 0.f);
     *reinterpret_cast<uint4*>(vdst + (int64_t)d * BN + k8) = *reinterpret_cast<uint4*>(t8);
   }
 }
@@ -257,6 +265,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return r;
+}
+
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(r) : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -277,10 +295,15 @@ constexpr uint32_t kIdesc = (1u << 4)                       // D format f32
                             | (0u << 7) | (0u << 10)        // A, B f16
                             | ((uint32_t)(pf::BN >> 3) << 17)   // N
                             | ((uint32_t)(pf::BM >> 4) << 24);  // M
+// P.V: N = 144 (128 output dims + the row-sum column + padding)
+constexpr uint32_t kIdescPV = (1u << 4) | ((uint32_t)(pf::VROWS >> 3) << 17) | ((uint32_t)(pf::BM >> 4) << 24);
 
 // ===========================================================================
 // attention kernel
 // ===========================================================================
+// MASK: general softmax input (additive mask and/or non-positive scale);
+// otherwise the max is taken on the raw scores and the scale is folded into
+// one FMA per score.
 template <bool MASK>
 __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams pp) {
   using namespace pf;
@@ -289,7 +312,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;
   uint8_t* sK = smem + TILE_BYTES;
-  uint8_t* sV = sK + KST * TILE_BYTES;
+  uint8_t* sV = sK + KST * TILE_BYTES;     // VST stages of VTILE_BYTES
   __shared__ __align__(8) uint64_t bar_q;
   __shared__ __align__(8) uint64_t bar_kfull[KST], bar_kempty[KST];
   __shared__ __align__(8) uint64_t bar_vfull[VST], bar_vempty[VST];
@@ -338,7 +361,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
     fence_barrier_init();
   }
   if (warp == 1) {
-    // allocate 512 tensor-memory columns: S0 S1 (0..255), O (256..383), P0 P1 (384..511)
+    // allocate 512 tensor-memory columns: S0 S1 (0..255; P_j is written as
+    // packed fp16 over the first 64 columns of S_j), O (256..399: 128 output
+    // columns, the row sum, padding)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;"
                  ::"r"(smem_u32(&tmem_base_sh)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -349,7 +374,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   const uint32_t tmem = tmem_base_sh;
   const uint32_t tS[2] = {tmem, tmem + 128};
   const uint32_t tO = tmem + 256;
-  const uint32_t tP[2] = {tmem + 384, tmem + 448};
+  const uint32_t tP[2] = {tS[0], tS[1]};
 
   if (nkv > 0) {
     if (warp == 0) {
@@ -367,10 +392,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
           tma_load_2d(kd + TILE_BYTES / 2, &pp.tm_k, 64, k_row_g + j * BN, &bar_kfull[ks]);
           const int vs = j % VST;
           if (j >= VST && !mbar_wait(&bar_vempty[vs], ((j / VST) - 1) & 1)) { abort_flag = 1; break; }
-          uint8_t* vd = sV + vs * TILE_BYTES;
-          mbar_arrive_expect_tx(&bar_vfull[vs], TILE_BYTES);
-          tma_load_2d(vd, &pp.tm_v, 0, (v_tile_g + j) * D, &bar_vfull[vs]);
-          tma_load_2d(vd + TILE_BYTES / 2, &pp.tm_v, 64, (v_tile_g + j) * D, &bar_vfull[vs]);
+          uint8_t* vd = sV + vs * VTILE_BYTES;
+          mbar_arrive_expect_tx(&bar_vfull[vs], VTILE_BYTES);
+          tma_load_2d(vd, &pp.tm_v, 0, (v_tile_g + j) * VROWS, &bar_vfull[vs]);
+          tma_load_2d(vd + VTILE_BYTES / 2, &pp.tm_v, 64, (v_tile_g + j) * VROWS, &bar_vfull[vs]);
         }
       }
     } else if (warp == 1) {
@@ -395,17 +420,19 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         tc_fence_after();
         ok = ok && issue_s(0);
         if (ok && nkv > 1) ok = issue_s(1);
+        // MMAs of one thread run in issue order, so S_{j+2} (issued after
+        // PV_j) cannot overwrite P_j before PV_j has read it.
         for (int j = 0; ok && j < nkv; ++j) {
           // O += P_j V_j
           const int vs = j % VST;
           if (!mbar_wait(&bar_p[j & 1], (j >> 1) & 1)) { ok = false; break; }
           if (!mbar_wait(&bar_vfull[vs], (j / VST) & 1)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t v_s = smem_u32(sV + vs * TILE_BYTES);
+          const uint32_t v_s = smem_u32(sV + vs * VTILE_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
-            tc_mma_ts(tO, tP[j & 1] + kk * 8, sw128_desc(v_s + off), kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t off = (kk >> 2) * (VTILE_BYTES / 2) + (kk & 3) * 32;
+            tc_mma_ts(tO, tP[j & 1] + kk * 8, sw128_desc(v_s + off), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&bar_vempty[vs]);
           tc_commit(&bar_o[j & 1]);
@@ -423,7 +450,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
       int row_end = kv_len;                                 // keys this row sees
       if (p.q_abs) row_end = min(row_end, max(0, qabs + t + 1));
       if (!row_valid) row_end = 0;
-      float m_run = -INFINITY, l_run = 0.f;
+      float m_run = -INFINITY;                              // log2 units, scale applied
       bool alive = true;
       for (int j = 0; j < nkv && alive; ++j) {
         if (!mbar_wait(&bar_s[j & 1], (j >> 1) & 1)) alive = false;
@@ -436,33 +463,39 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         const int k0 = j * BN;
         const bool need_mask = MASK || (k0 + BN > key_full) || !row_valid;
         float mx = -INFINITY;
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            float x = __uint_as_float(s[c][e]) * pp.scale_log2;
-            if (need_mask) {
-              const int k = k0 + c * 32 + e;
+            for (int e = 0; e < 32; ++e) {
+              float x = __uint_as_float(s[c][e]);
               if constexpr (MASK) {
-                if (row_valid && k < kv_len)
+                x *= pp.scale_log2;
+                const int k = k0 + c * 32 + e;
+                if (p.mask && row_valid && k < kv_len)
                   x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
                       (int64_t)b * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
               }
-              if (k >= row_end) x = -INFINITY;
+              if (k0 + c * 32 + e >= row_end) x = -INFINITY;
+              s[c][e] = __float_as_uint(x);
+              mx = fmaxf(mx, x);
             }
-            s[c][e] = __float_as_uint(x);
-            mx = fmaxf(mx, x);
-          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(s[c][e]));
+        }
+        if constexpr (!MASK) mx *= pp.scale_log2;   // scale > 0: max commutes with the scale
         // lazy rescale: keep the old max unless the new one exceeds it by
         // more than 2^8.  tcgen05.ld/st are warp-collective, so the O
         // rescale is decided by a warp vote; rows that do not need it scale
-        // by 1.
+        // by 1.  O's column 128 holds the row sum and is rescaled with it.
         float alpha = 1.f;
         bool rescale_o = false;
         if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleThreshold)) {
           if (m_run != -INFINITY) {
             alpha = fast_exp2(m_run - mx);
-            l_run *= alpha;
             rescale_o = j > 0;
           }
           m_run = mx;
@@ -481,19 +514,25 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
             tmem_st32(tO + lane_off + c * 32, o);
           }
+          const uint32_t lsum = tmem_ld1(tO + lane_off + D);
+          tmem_wait_ld();
+          tmem_st1(tO + lane_off + D, __float_as_uint(__uint_as_float(lsum) * alpha));
           tmem_wait_st();
         }
+        // P = 2^(x - m) in fp16: the exponent is taken on packed pairs
+        // (ex2.approx.f16x2), one MUFU issue per two keys.  The fp16 P is the
+        // one both P.V and the row sum (ones row of V^T) use.
         const float mu = m_run == -INFINITY ? 0.f : m_run;
-        float ls = 0.f;
+        const float sc = MASK ? 1.f : pp.scale_log2;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e) {
-            const float p0 = fast_exp2(__uint_as_float(s[c][2 * e]) - mu);
-            const float p1 = fast_exp2(__uint_as_float(s[c][2 * e + 1]) - mu);
-            ls += p0 + p1;
-            pk[e] = pack_half2(p0, p1);
+            const float x0 = fmaf(__uint_as_float(s[c][2 * e]), sc, -mu);
+            const float x1 = fmaf(__uint_as_float(s[c][2 * e + 1]), sc, -mu);
+            const __half2 h = h2exp2(__floats2half2_rn(x0, x1));
+            pk[e] = *reinterpret_cast<const uint32_t*>(&h);
           }
           // 16 packed columns per 32 keys
           asm volatile(
@@ -503,7 +542,6 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
                 "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
               : "memory");
         }
-        l_run += ls;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bar_p[j & 1]);
@@ -512,7 +550,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
       // PV_{nkv-1} completing implies every earlier MMA completed
       if (alive && mbar_wait(&bar_o[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1)) {
         tc_fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        const float l_row = __uint_as_float(tmem_ld1(tO + lane_off + D));
+        tmem_wait_ld();
+        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
         const int g = rg - t * pp.G;
         const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
 #pragma unroll
@@ -569,13 +609,13 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2-D fp16 tensor [rows][128], box 64 x 128 rows, 128-byte swizzle
-static bool make_tmap(CUtensorMap* tm, const void* base, int64_t rows) {
+// 2-D fp16 tensor [rows][128], box 64 x box_rows, 128-byte swizzle
+static bool make_tmap(CUtensorMap* tm, const void* base, int64_t rows, int box_rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   cuuint64_t dims[2] = {(cuuint64_t)pf::D, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)pf::D * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t es[2] = {1, 1};
   return enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -598,7 +638,7 @@ static PrefillPlan plan_prefill(const G9AttnBatch& p, int nseq, const int* nq_ca
   const size_t tile = (size_t)pf::TILE_BYTES;
   pl.q_bytes = (size_t)p.num_heads_kv * pl.RT * tile;
   pl.k_bytes = (size_t)p.num_heads_kv * pl.KT * tile;
-  pl.v_bytes = pl.k_bytes;
+  pl.v_bytes = (size_t)p.num_heads_kv * pl.KT * pf::VTILE_BYTES;
   pl.total = pl.q_bytes + pl.k_bytes + pl.v_bytes + 1024;
   return pl;
 }
@@ -651,9 +691,9 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     pp.qp = reinterpret_cast<__half*>(w);
     pp.kp = reinterpret_cast<__half*>(w + pl.q_bytes);
     pp.vt = reinterpret_cast<__half*>(w + pl.q_bytes + pl.k_bytes);
-    if (!make_tmap(&pp.tm_q, pp.qp, (int64_t)pp.Hkv * pp.RT * BM) ||
-        !make_tmap(&pp.tm_k, pp.kp, (int64_t)pp.Hkv * std::max(pp.KT, 1) * BN) ||
-        !make_tmap(&pp.tm_v, pp.vt, (int64_t)pp.Hkv * std::max(pp.KT, 1) * D))
+    if (!make_tmap(&pp.tm_q, pp.qp, (int64_t)pp.Hkv * pp.RT * BM, BM) ||
+        !make_tmap(&pp.tm_k, pp.kp, (int64_t)pp.Hkv * std::max(pp.KT, 1) * BN, BN) ||
+        !make_tmap(&pp.tm_v, pp.vt, (int64_t)pp.Hkv * std::max(pp.KT, 1) * VROWS, VROWS))
       return cudaErrorInvalidValue;
     if (pp.KT > 0) {
       pack_kv_kernel<<<dim3(pp.KT, pp.Hkv), 256, 0, stream>>>(pp);
@@ -661,8 +701,8 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     }
     pack_q_kernel<<<dim3(pp.RT, pp.Hkv), 256, 0, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t smem = (size_t)(1 + KST + VST) * TILE_BYTES + 1024;
-    auto kern = p.mask ? prefill_kernel<true> : prefill_kernel<false>;
+    const size_t smem = (size_t)(1 + KST) * TILE_BYTES + (size_t)VST * VTILE_BYTES + 1024;
+    auto kern = (p.mask || !(p.scale > 0.f)) ? prefill_kernel<true> : prefill_kernel<false>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
       return e;
     kern<<<pp.Hkv * pp.RT, NTHREADS, smem, stream>>>(pp);
