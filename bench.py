@@ -139,6 +139,14 @@ def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
     return k_cache, v_cache, bt
 
 
+# DRAM bytes (read + write) of one decode_kernel launch per algorithmic byte:
+# ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum on the first 16
+# sequences of config 3 (fp16 V) read 666.97 MB and wrote 20.39 MB against
+# 666.14 MB of algorithmic bytes (K rows, V rows, Q, O, block table).  The
+# excess is the split-K partials.
+DECODE_TRAFFIC_RATIO = (666.97 + 20.39) / 666.14
+
+
 def decode_bytes(lens, hkv, hq, v_row=256):
     kv = int(np.sum(lens)) * hkv * (RB + v_row)
     q = len(lens) * hq * D * 2
@@ -380,12 +388,15 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 Q / q8_0 K / "
             + ("q8_0" if args.v_fmt == "q8_0" else "fp16") + " V, fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": "config3 decode: 64 seqs x 1 query, L~U[1K,32K] seed 3, GQA 48/8, d128, "
+            "config": {"workload": f"config3 decode: {B} seqs x 1 query, L~U[1K,32K] seed 3, GQA 48/8, d128, "
                                    "block 16, shuffled pages",
                        "kv_heads_per_gpu": hkv, "parallelism": f"kv-head groups x{world}",
                        "l2": "inputs (%.2f GB per GPU) larger than L2, no flush" % (bytes_rank / 1e9)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None,
+                         "frac": achieved / hbm_peak,
+                         "traffic": bytes_rank * DECODE_TRAFFIC_RATIO,
+                         "traffic_note": "ncu dram read+write of decode_kernel on the 16-sequence prefix of "
+                                         "this workload, scaled by the algorithmic bytes",
                          "peak_kind": f"{peak_kind} copy bandwidth"},
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "path": "gfx906_fa_paged.forward_paged (reference plugin API), pinned host Q in, O out"},
