@@ -10,27 +10,26 @@
 //
 //  1. pack (CUDA cores, HBM-bound): the Q8_0 pages a prefill sequence can
 //     see are dequantised ONCE per call into fp16 staging tiles -- K as
-//     [key][d] rows, V transposed as [d][key] 144x128 tiles (V^T, ones, zeros) -- and Q is
+//     [key][d] rows, V transposed as [d][key] 128x128 tiles -- and Q is
 //     converted to fp16 with the GQA group packed into rows (row = t*G + g).
 //     Dequantisation is one rounding: q8 * d computed in fp32, rounded to
 //     fp16.  Doing it once per call instead of once per (query tile, kv
 //     tile) pair keeps the conversion work out of the tensor-core loop,
 //     where it would compete with the softmax for issue slots.
 //
-//  2. attention (tcgen05): one CTA per 128 packed query rows of one kv head.
-//     warp 0 drives TMA (128-byte swizzled tiles), warp 1 allocates tensor
-//     memory and issues tcgen05.mma from one thread, warps 4-7 run the
-//     softmax with one thread per query row (row i = TMEM lane i).  Tensor
-//     memory: S double-buffered (2 x 128 fp32 columns); P_j is written as
-//     packed fp16 over the first 64 columns of S_j; O has 144 columns.
-//     S = Q K^T reads both operands from shared memory; O += P V reads P
-//     from tensor memory and V^T from shared memory.  Each V^T tile carries
-//     a row of ones after its 128 dims, so column 128 of O accumulates the
-//     softmax row sums on the tensor core from the same fp16 P.  The MMA
-//     order S0 S1 PV0 S2 PV1 ... lets the next S tile run while the softmax
-//     works on the current one.  Exponentials are taken on fp16 pairs
-//     (ex2.approx.f16x2).  The running max is rescaled lazily (only when it
-//     grows by more than 2^8), so O is rarely touched by the softmax warps.
+//  2. attention (tcgen05): one CTA per two 128-row query tiles (256 packed
+//     rows) of one kv head, so every K/V tile loaded by TMA (128-byte
+//     swizzled) feeds two tiles of MMAs.  warp 0 drives TMA, warp 1 allocates
+//     tensor memory and issues tcgen05.mma from one thread, and two softmax
+//     warpgroups (one per query tile) run one thread per query row (row i =
+//     TMEM lane i).  Tensor memory: S0 S1 (128 fp32 columns each; P_i is
+//     written as packed fp16 over S_i), O0 O1 (128 columns each).  The MMA
+//     order PV0(j) S0(j+1) PV1(j) S1(j+1) keeps the tensor core on one tile
+//     while the other tile's softmax runs.  Exponentials are split between
+//     MUFU (ex2.approx) and a polynomial on the FMA pipe (one pair in four)
+//     so that neither pipe limits the tensor core.  The running max is
+//     rescaled lazily (only when it grows by more than 2^8), so O is rarely
+//     touched by the softmax warps.
 //
 // Masking is the reference's: keys k >= kv_len ignored; causal rule
 // k <= q_abs[b] + t (fattn-q8.cuh:646-654); optional fp16 additive mask.
@@ -46,15 +45,19 @@ namespace g9 {
 
 namespace pf {
 constexpr int D = 128;
-constexpr int BM = 128;          // query rows per CTA
+constexpr int BM = 128;          // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;          // keys per tile
 constexpr int KST = 3;           // K smem stages
 constexpr int VST = 2;           // V smem stages
 constexpr int TILE_BYTES = BM * D * 2;   // 32 KB (Q and K tiles)
-constexpr int VROWS = D + 16;            // V^T tile rows: 128 dims + a row of ones + 15 zero rows
-constexpr int VTILE_BYTES = VROWS * BN * 2;   // 36 KB
+static_assert(D == BN, "V^T tiles share the K tiles' row coordinates");
 constexpr int MAXS = 128;        // prefill sequences per launch
-constexpr int NTHREADS = 256;
+// warp 0: TMA, warp 1: MMA, warps 4-7 / 8-11: softmax of query tile 0 / 1.
+// setmaxnreg split: launch 384 threads x 168 = 64512 = 128*REG_CTRL + 256*REG_SOFTMAX
+constexpr int NTHREADS = 384;
+constexpr int REG_CTRL = 72;
+constexpr int REG_SOFTMAX = 216;
+static_assert(128 * REG_CTRL + 256 * REG_SOFTMAX <= NTHREADS * 168, "register split exceeds the launch budget");
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 }  // namespace pf
 
@@ -73,7 +76,7 @@ struct PrefillParams {
   float scale_log2;
   __half* qp;                    // [Hkv][RT*128][128]
   __half* kp;                    // [Hkv][KT*128][128]
-  __half* vt;                    // [Hkv][KT][144][128 keys]: V^T, then ones, then zeros
+  __half* vt;                    // [Hkv][KT][128 d][128 keys]: V^T tiles
 };
 
 __device__ __forceinline__ int find_seq(const int* off, int n, int x) {
@@ -157,16 +160,14 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
   }
   __syncthreads();
   // transposed write: V^T tile [d][key], 8 keys (16 bytes) per item
-  // rows 0..127: V^T; row 128: ones, so that the P.V product also yields the
-  // softmax row sums in fp32; rows 129..143: zeros (N must be a multiple of 16)
-  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)VROWS * BN;
-  for (int it = threadIdx.x; it < VROWS * (BN / 8); it += blockDim.x) {
+  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)D * BN;
+  for (int it = threadIdx.x; it < D * (BN / 8); it += blockDim.x) {
     const int d = it / (BN / 8);
     const int k8 = (it % (BN / 8)) * 8;
     __align__(16) __half t8[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e)
-      t8[e] = d < D ? vs[k8 + e][d] : __float2half_rn(d == D ? 1.f : 0.f);
+      t8[e] = vs[k8 + e][d];
     *reinterpret_cast<uint4*>(vdst + (int64_t)d * BN + k8) = *reinterpret_cast<uint4*>(t8);
   }
 }
@@ -295,30 +296,63 @@ constexpr uint32_t kIdesc = (1u << 4)                       // D format f32
                             | (0u << 7) | (0u << 10)        // A, B f16
                             | ((uint32_t)(pf::BN >> 3) << 17)   // N
                             | ((uint32_t)(pf::BM >> 4) << 24);  // M
-// P.V: N = 144 (128 output dims + the row-sum column + padding)
-constexpr uint32_t kIdescPV = (1u << 4) | ((uint32_t)(pf::VROWS >> 3) << 17) | ((uint32_t)(pf::BM >> 4) << 24);
 
 // ===========================================================================
 // attention kernel
 // ===========================================================================
+// 2^x on the FMA pipe for x <= 2^7 (Cody-Waite split into floor and
+// fraction, then a degree-3 minimax polynomial for 2^f on [0, 1), relative
+// error 7.5e-5, below the fp16 rounding of P).  floor(x) comes from adding
+// 1.5 * 2^23 with round-down, which leaves it in the low mantissa bits;
+// shifting those bits into the exponent field scales the polynomial.  Inputs
+// below -126 (including -inf) are clamped to -126: the polynomial lies in
+// [0.99992, 2), so its exponent field stays >= 0 (a denormal at most, which
+// rounds to 0 in fp16) and never borrows into the sign bit.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rd(x, 12582912.f);
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.07802300900220871f, f, 0.2260693907737732f), f, 0.6958328485488892f), f,
+                       0.9999252557754517f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // MASK: general softmax input (additive mask and/or non-positive scale);
 // otherwise the max is taken on the raw scores and the scale is folded into
 // one FMA per score.
+//
+// CTA = two 128-row query tiles of one kv head sharing every K/V tile.
+// warp 0: TMA producer; warp 1: TMEM owner and MMA issuer (warps 0-3 give
+// registers to the softmax warpgroups through setmaxnreg); warps 4-7:
+// softmax of tile 0, warps 8-11: softmax of tile 1 (thread = row = TMEM
+// lane; warp w reaches TMEM lanes 32*(w % 4) .. +31).  Tensor memory: S0 S1 (P_i written as packed
+// fp16 over the first 64 columns of S_i), O0 O1.  MMA order per key tile j:
+//   PV0(j)  S0(j+1)  PV1(j)  S1(j+1)
+// so the tensor core works on one tile while the other tile's softmax runs.
+// Tile i's S(j+1) is issued after its PV(j), which (MMAs of one thread run in
+// issue order) both protects P_i(j) and means that when the softmax sees
+// S_i(j+1) complete, O_i holds every PV before it and may be rescaled.
 template <bool MASK>
 __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_constant__ PrefillParams pp) {
   using namespace pf;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + TILE_BYTES;
-  uint8_t* sV = sK + KST * TILE_BYTES;     // VST stages of VTILE_BYTES
+  uint8_t* sQ = smem;                        // 2 tiles
+  uint8_t* sK = smem + 2 * TILE_BYTES;
+  uint8_t* sV = sK + KST * TILE_BYTES;
   __shared__ __align__(8) uint64_t bar_q;
   __shared__ __align__(8) uint64_t bar_kfull[KST], bar_kempty[KST];
   __shared__ __align__(8) uint64_t bar_vfull[VST], bar_vempty[VST];
-  __shared__ __align__(8) uint64_t bar_s[2];     // S tile ready (MMA -> softmax)
-  __shared__ __align__(8) uint64_t bar_p[2];     // P tile ready (softmax -> MMA)
-  __shared__ __align__(8) uint64_t bar_o[2];     // PV_j finished (barrier j & 1)
+  __shared__ __align__(8) uint64_t bar_s[2];     // S_i tile ready (MMA -> softmax i)
+  __shared__ __align__(8) uint64_t bar_p[2];     // P_i tile ready (softmax i -> MMA)
+  __shared__ __align__(8) uint64_t bar_o[2];     // last PV_i finished
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
 
@@ -326,10 +360,10 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   const int warp = warp_id();
   const int lane = lane_id();
 
-  // ---- work item: heavy (late) row tiles first --------------------------------
+  // ---- work item: heavy (late) row-tile pairs first ---------------------------
   const int idx = blockIdx.x;
   const int h = idx % pp.Hkv;
-  const int grt = pp.RT - 1 - idx / pp.Hkv;               // global row tile
+  const int grt = pp.RT - 2 - 2 * (idx / pp.Hkv);          // first global row tile of the pair
   const int si = find_seq(pp.rtile_off, pp.nseq, grt);
   const int m = grt - pp.rtile_off[si];
   const int b = pp.seq_b[si];
@@ -338,19 +372,14 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   const int kv_len = p.kv_len[b];
   const int qabs = p.q_abs ? p.q_abs[b] : 0;
   const int row0 = m * BM;
-  if (row0 >= R || R <= pp.min_rows) return;              // padding tile / decode-sized sequence
-  const int t_lo = row0 / pp.G;
-  const int t_hi = min(nq - 1, (row0 + BM - 1) / pp.G);
-  int key_end = kv_len;                                    // keys any row of the tile sees
-  int key_full = kv_len;                                   // keys every row sees
-  if (p.q_abs) {
-    key_end = min(key_end, max(0, qabs + t_hi + 1));
-    key_full = min(key_full, max(0, qabs + t_lo + 1));
-  }
+  if (row0 >= R || R <= pp.min_rows) return;              // padding pair / decode-sized sequence
+  const bool has1 = row0 + BM < R;                         // second tile holds rows
+  const int t_hi = min(nq - 1, (row0 + 2 * BM - 1) / pp.G);
+  int key_end = kv_len;                                    // keys any row of the pair sees
+  if (p.q_abs) key_end = min(key_end, max(0, qabs + t_hi + 1));
   const int nkv = (key_end + BN - 1) / BN;
-  const int q_row_g = (h * pp.RT + pp.rtile_off[si] + m) * BM;
+  const int q_row_g = (h * pp.RT + grt) * BM;
   const int k_row_g = (h * pp.KT + pp.ktile_off[si]) * BN;
-  const int v_tile_g = h * pp.KT + pp.ktile_off[si];
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_q, 1);
@@ -361,9 +390,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
     fence_barrier_init();
   }
   if (warp == 1) {
-    // allocate 512 tensor-memory columns: S0 S1 (0..255; P_j is written as
-    // packed fp16 over the first 64 columns of S_j), O (256..399: 128 output
-    // columns, the row sum, padding)
+    // 512 tensor-memory columns: S0 (0..127), S1 (128..255), O0 (256..383), O1 (384..511)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;"
                  ::"r"(smem_u32(&tmem_base_sh)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -372,187 +399,193 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
-  const uint32_t tP[2] = {tS[0], tS[1]};
 
-  if (nkv > 0) {
-    if (warp == 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
+    if (nkv > 0 && warp == 0 && lane == 0) {
       // ======================= TMA producer ==================================
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&bar_q, TILE_BYTES);
-        tma_load_2d(sQ, &pp.tm_q, 0, q_row_g, &bar_q);
-        tma_load_2d(sQ + TILE_BYTES / 2, &pp.tm_q, 64, q_row_g, &bar_q);
-        for (int j = 0; j < nkv; ++j) {
-          const int ks = j % KST;
-          if (j >= KST && !mbar_wait(&bar_kempty[ks], ((j / KST) - 1) & 1)) { abort_flag = 1; break; }
-          uint8_t* kd = sK + ks * TILE_BYTES;
-          mbar_arrive_expect_tx(&bar_kfull[ks], TILE_BYTES);
-          tma_load_2d(kd, &pp.tm_k, 0, k_row_g + j * BN, &bar_kfull[ks]);
-          tma_load_2d(kd + TILE_BYTES / 2, &pp.tm_k, 64, k_row_g + j * BN, &bar_kfull[ks]);
-          const int vs = j % VST;
-          if (j >= VST && !mbar_wait(&bar_vempty[vs], ((j / VST) - 1) & 1)) { abort_flag = 1; break; }
-          uint8_t* vd = sV + vs * VTILE_BYTES;
-          mbar_arrive_expect_tx(&bar_vfull[vs], VTILE_BYTES);
-          tma_load_2d(vd, &pp.tm_v, 0, (v_tile_g + j) * VROWS, &bar_vfull[vs]);
-          tma_load_2d(vd + VTILE_BYTES / 2, &pp.tm_v, 64, (v_tile_g + j) * VROWS, &bar_vfull[vs]);
-        }
+      mbar_arrive_expect_tx(&bar_q, 2 * TILE_BYTES);
+      for (int i = 0; i < 2; ++i) {
+        tma_load_2d(sQ + i * TILE_BYTES, &pp.tm_q, 0, q_row_g + i * BM, &bar_q);
+        tma_load_2d(sQ + i * TILE_BYTES + TILE_BYTES / 2, &pp.tm_q, 64, q_row_g + i * BM, &bar_q);
       }
-    } else if (warp == 1) {
+      for (int j = 0; j < nkv; ++j) {
+        const int ks = j % KST;
+        if (j >= KST && !mbar_wait(&bar_kempty[ks], ((j / KST) - 1) & 1)) { abort_flag = 1; break; }
+        uint8_t* kd = sK + ks * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar_kfull[ks], TILE_BYTES);
+        tma_load_2d(kd, &pp.tm_k, 0, k_row_g + j * BN, &bar_kfull[ks]);
+        tma_load_2d(kd + TILE_BYTES / 2, &pp.tm_k, 64, k_row_g + j * BN, &bar_kfull[ks]);
+        const int vs = j % VST;
+        if (j >= VST && !mbar_wait(&bar_vempty[vs], ((j / VST) - 1) & 1)) { abort_flag = 1; break; }
+        uint8_t* vd = sV + vs * TILE_BYTES;
+        mbar_arrive_expect_tx(&bar_vfull[vs], TILE_BYTES);
+        tma_load_2d(vd, &pp.tm_v, 0, k_row_g + j * BN, &bar_vfull[vs]);
+        tma_load_2d(vd + TILE_BYTES / 2, &pp.tm_v, 64, k_row_g + j * BN, &bar_vfull[vs]);
+      }
+    } else if (nkv > 0 && warp == 1 && lane == 0) {
       // ======================= MMA issuer ====================================
-      if (lane == 0) {
-        const uint32_t q_s = smem_u32(sQ);
-        auto issue_s = [&](int j) -> bool {
-          const int ks = j % KST;
-          if (!mbar_wait(&bar_kfull[ks], (j / KST) & 1)) return false;
-          tc_fence_after();
-          const uint32_t k_s = smem_u32(sK + ks * TILE_BYTES);
+      const uint32_t q_s = smem_u32(sQ);
+      auto issue_s = [&](int i, int j) {
+        const uint32_t k_s = smem_u32(sK + (j % KST) * TILE_BYTES);
+        const uint32_t qi = q_s + i * TILE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
-            tc_mma_ss(tS[j & 1], sw128_desc(q_s + off), sw128_desc(k_s + off), kIdesc, kk > 0);
-          }
-          tc_commit(&bar_kempty[ks]);     // K stage free once this S is done
-          tc_commit(&bar_s[j & 1]);       // S tile ready
-          return true;
-        };
-        bool ok = mbar_wait(&bar_q, 0);
-        tc_fence_after();
-        ok = ok && issue_s(0);
-        if (ok && nkv > 1) ok = issue_s(1);
-        // MMAs of one thread run in issue order, so S_{j+2} (issued after
-        // PV_j) cannot overwrite P_j before PV_j has read it.
-        for (int j = 0; ok && j < nkv; ++j) {
-          // O += P_j V_j
-          const int vs = j % VST;
-          if (!mbar_wait(&bar_p[j & 1], (j >> 1) & 1)) { ok = false; break; }
-          if (!mbar_wait(&bar_vfull[vs], (j / VST) & 1)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t v_s = smem_u32(sV + vs * VTILE_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (VTILE_BYTES / 2) + (kk & 3) * 32;
-            tc_mma_ts(tO, tP[j & 1] + kk * 8, sw128_desc(v_s + off), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(&bar_vempty[vs]);
-          tc_commit(&bar_o[j & 1]);
-          if (j + 2 < nkv) ok = issue_s(j + 2);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
+          tc_mma_ss(tmem + i * 128, sw128_desc(qi + off), sw128_desc(k_s + off), kIdesc, kk > 0);
         }
-        if (!ok) abort_flag = 1;
+        tc_commit(&bar_s[i]);
+      };
+      auto issue_pv = [&](int i, int j) {
+        const uint32_t v_s = smem_u32(sV + (j % VST) * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
+          tc_mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, sw128_desc(v_s + off), kIdesc,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(&bar_q, 0) && mbar_wait(&bar_kfull[0], 0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (has1) issue_s(1, 0);
+        tc_commit(&bar_kempty[0]);
       }
-    } else if (warp >= 4) {
-      // ======================= softmax (one thread per row) ==================
-      const int r = (warp - 4) * 32 + lane;                 // TMEM lane == row
-      const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
-      const int rg = row0 + r;
-      const int t = rg / pp.G;
-      const bool row_valid = rg < R;
-      int row_end = kv_len;                                 // keys this row sees
-      if (p.q_abs) row_end = min(row_end, max(0, qabs + t + 1));
-      if (!row_valid) row_end = 0;
-      float m_run = -INFINITY;                              // log2 units, scale applied
-      bool alive = true;
-      for (int j = 0; j < nkv && alive; ++j) {
-        if (!mbar_wait(&bar_s[j & 1], (j >> 1) & 1)) alive = false;
-        if (!__all_sync(0xffffffffu, alive)) { alive = false; break; }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const bool more = j + 1 < nkv;
+        if (!mbar_wait(&bar_vfull[j % VST], (j / VST) & 1)) { ok = false; break; }
+        if (more && !mbar_wait(&bar_kfull[(j + 1) % KST], ((j + 1) / KST) & 1)) { ok = false; break; }
+        if (!mbar_wait(&bar_p[0], j & 1)) { ok = false; break; }
         tc_fence_after();
-        uint32_t s[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tS[j & 1] + lane_off + c * 32, s[c]);
-        tmem_wait_ld();
-        const int k0 = j * BN;
-        const bool need_mask = MASK || (k0 + BN > key_full) || !row_valid;
-        float mx = -INFINITY;
-        if (need_mask) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              float x = __uint_as_float(s[c][e]);
-              if constexpr (MASK) {
-                x *= pp.scale_log2;
-                const int k = k0 + c * 32 + e;
-                if (p.mask && row_valid && k < kv_len)
-                  x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
-                      (int64_t)b * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
-              }
-              if (k0 + c * 32 + e >= row_end) x = -INFINITY;
-              s[c][e] = __float_as_uint(x);
-              mx = fmaxf(mx, x);
-            }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(s[c][e]));
-        }
-        if constexpr (!MASK) mx *= pp.scale_log2;   // scale > 0: max commutes with the scale
-        // lazy rescale: keep the old max unless the new one exceeds it by
-        // more than 2^8.  tcgen05.ld/st are warp-collective, so the O
-        // rescale is decided by a warp vote; rows that do not need it scale
-        // by 1.  O's column 128 holds the row sum and is rescaled with it.
-        float alpha = 1.f;
-        bool rescale_o = false;
-        if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleThreshold)) {
-          if (m_run != -INFINITY) {
-            alpha = fast_exp2(m_run - mx);
-            rescale_o = j > 0;
-          }
-          m_run = mx;
-        }
-        if (__any_sync(0xffffffffu, rescale_o)) {
-          // O holds PV_0 .. PV_{j-1}; wait for PV_{j-1}, then rescale in place
-          if (!mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1)) alive = false;
-          if (!__all_sync(0xffffffffu, alive)) { alive = false; break; }
+        issue_pv(0, j);
+        if (more) issue_s(0, j + 1);
+        if (has1) {
+          if (!mbar_wait(&bar_p[1], j & 1)) { ok = false; break; }
           tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tO + lane_off + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, o);
-          }
-          const uint32_t lsum = tmem_ld1(tO + lane_off + D);
-          tmem_wait_ld();
-          tmem_st1(tO + lane_off + D, __float_as_uint(__uint_as_float(lsum) * alpha));
-          tmem_wait_st();
+          issue_pv(1, j);
+          if (more) issue_s(1, j + 1);
         }
-        // P = 2^(x - m) in fp16: the exponent is taken on packed pairs
-        // (ex2.approx.f16x2), one MUFU issue per two keys.  The fp16 P is the
-        // one both P.V and the row sum (ones row of V^T) use.
-        const float mu = m_run == -INFINITY ? 0.f : m_run;
-        const float sc = MASK ? 1.f : pp.scale_log2;
+        tc_commit(&bar_vempty[j % VST]);
+        if (more) tc_commit(&bar_kempty[(j + 1) % KST]);
+      }
+      if (ok) { tc_commit(&bar_o[0]); tc_commit(&bar_o[1]); }
+      if (!ok) abort_flag = 1;
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFTMAX));
+    const int wi = (warp - 4) >> 2;                        // query tile of this warpgroup
+    const int r = (warp & 3) * 32 + lane;                  // TMEM lane == row
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + wi * 128;
+    const uint32_t tO = tmem + 256 + wi * 128;
+    const int rg = row0 + wi * BM + r;
+    const int t = rg / pp.G;
+    const bool row_valid = rg < R;
+    int row_end = kv_len;                                  // keys this row sees
+    if (p.q_abs) row_end = min(row_end, max(0, qabs + t + 1));
+    if (!row_valid) row_end = 0;
+    // keys every row of this tile sees
+    int key_full = kv_len;
+    if (p.q_abs) key_full = min(key_full, max(0, qabs + (row0 + wi * BM) / pp.G + 1));
+    const bool active = nkv > 0 && (wi == 0 || has1);
+    float m_run = -INFINITY, l_run = 0.f;                  // log2 units, scale applied
+    bool alive = true;
+    for (int j = 0; active && j < nkv && alive; ++j) {
+      if (!mbar_wait(&bar_s[wi], j & 1)) alive = false;
+      if (!__all_sync(0xffffffffu, alive)) { alive = false; break; }
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, s[c]);
+      tmem_wait_ld();
+      const int k0 = j * BN;
+      const bool need_mask = MASK || (k0 + BN > key_full) || !row_valid;
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            float x = __uint_as_float(s[c][e]);
+            if constexpr (MASK) {
+              x *= pp.scale_log2;
+              const int k = k0 + c * 32 + e;
+              if (p.mask && row_valid && k < kv_len)
+                x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                    (int64_t)b * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+            }
+            if (k0 + c * 32 + e >= row_end) x = -INFINITY;
+            s[c][e] = __float_as_uint(x);
+          }
+      }
+      float mc[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        mc[c] = __uint_as_float(s[c][0]);
+#pragma unroll
+        for (int e = 1; e < 31; e += 2) mc[c] = fmax3(mc[c], __uint_as_float(s[c][e]), __uint_as_float(s[c][e + 1]));
+        mc[c] = fmaxf(mc[c], __uint_as_float(s[c][31]));
+      }
+      float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3]));
+      if constexpr (!MASK) mx *= pp.scale_log2;   // scale > 0: max commutes with the scale
+      // lazy rescale: keep the old max unless the new one exceeds it by
+      // more than 2^8.  tcgen05.ld/st are warp-collective, so the O rescale
+      // is decided by a warp vote; rows that do not need it scale by 1.
+      float alpha = 1.f;
+      bool rescale_o = false;
+      if (mx != -INFINITY && (m_run == -INFINITY || mx > m_run + kRescaleThreshold)) {
+        if (m_run != -INFINITY) {
+          alpha = fast_exp2(m_run - mx);
+          l_run *= alpha;
+          rescale_o = j > 0;
+        }
+        m_run = mx;
+      }
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // S_i(j) complete => every earlier PV_i complete: rescale O_i in place
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t pk[16];
+          uint32_t o[32];
+          tmem_ld32(tO + lane_off + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float x0 = fmaf(__uint_as_float(s[c][2 * e]), sc, -mu);
-            const float x1 = fmaf(__uint_as_float(s[c][2 * e + 1]), sc, -mu);
-            const __half2 h = h2exp2(__floats2half2_rn(x0, x1));
-            pk[e] = *reinterpret_cast<const uint32_t*>(&h);
-          }
-          // 16 packed columns per 32 keys
-          asm volatile(
-              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-              ::"r"(tP[j & 1] + lane_off + c * 16), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]),
-                "r"(pk[5]), "r"(pk[6]), "r"(pk[7]), "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]),
-                "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
-              : "memory");
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + lane_off + c * 32, o);
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&bar_p[j & 1]);
       }
-      // ---- epilogue: O / l -> out -------------------------------------------------
-      // PV_{nkv-1} completing implies every earlier MMA completed
-      if (alive && mbar_wait(&bar_o[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1)) {
+      // P = 2^(x - m): one pair in four on the FMA pipe, the rest on MUFU
+      const float mu = m_run == -INFINITY ? 0.f : m_run;
+      const float sc = MASK ? 1.f : pp.scale_log2;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {                        // 16 keys -> 8 packed columns
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x0 = fmaf(__uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e]), sc, -mu);
+          const float x1 = fmaf(__uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e + 1]), sc, -mu);
+          float p0, p1;
+          if ((e & 3) == 3) { p0 = exp2_fma(x0); p1 = exp2_fma(x1); }
+          else { p0 = fast_exp2(x0); p1 = fast_exp2(x1); }
+          ls[c & 3] += p0 + p1;
+          pk[e] = pack_half2(p0, p1);
+        }
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+            ::"r"(tS + lane_off + c * 8), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]),
+              "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
+            : "memory");
+      }
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bar_p[wi]);
+    }
+    // ---- epilogue: O / l -> out ---------------------------------------------------
+    if (active) {
+      if (alive && mbar_wait(&bar_o[wi], 0)) {
         tc_fence_after();
-        const float l_row = __uint_as_float(tmem_ld1(tO + lane_off + D));
-        tmem_wait_ld();
-        const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         const int g = rg - t * pp.G;
         const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
 #pragma unroll
@@ -570,13 +603,8 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
       } else {
         abort_flag = 1;
       }
-    }
-  } else if (warp >= 4) {
-    // no visible key for any row of this tile: zeros
-    const int r = (warp - 4) * 32 + lane;
-    const int rg = row0 + r;
-    if (rg < R) {
-      const int t = rg / pp.G;
+    } else if (nkv == 0 && row_valid) {
+      // no visible key for any row of this pair: zeros
       const int64_t ob = o_offset(p, b, t, h * pp.G + (rg - t * pp.G));
       for (int e = 0; e < D; e += 2) store_out2(p.out, p.out_dtype, ob + e, 0.f, 0.f);
     }
@@ -632,13 +660,13 @@ static PrefillPlan plan_prefill(const G9AttnBatch& p, int nseq, const int* nq_ca
   PrefillPlan pl;
   const int G = p.num_heads_q / p.num_heads_kv;
   for (int i = 0; i < nseq; ++i) {
-    pl.RT += (int)(((int64_t)nq_cap[i] * G + pf::BM - 1) / pf::BM);
+    pl.RT += 2 * (int)(((int64_t)nq_cap[i] * G + 2 * pf::BM - 1) / (2 * pf::BM));   // whole tile pairs
     pl.KT += (kv_cap[i] + pf::BN - 1) / pf::BN;
   }
   const size_t tile = (size_t)pf::TILE_BYTES;
   pl.q_bytes = (size_t)p.num_heads_kv * pl.RT * tile;
   pl.k_bytes = (size_t)p.num_heads_kv * pl.KT * tile;
-  pl.v_bytes = (size_t)p.num_heads_kv * pl.KT * pf::VTILE_BYTES;
+  pl.v_bytes = pl.k_bytes;
   pl.total = pl.q_bytes + pl.k_bytes + pl.v_bytes + 1024;
   return pl;
 }
@@ -680,7 +708,7 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
       pp.seq_b[i] = seq_ids[base + i];
       pp.rtile_off[i] = ro;
       pp.ktile_off[i] = ko;
-      ro += (int)(((int64_t)nq_cap[base + i] * pp.G + BM - 1) / BM);
+      ro += 2 * (int)(((int64_t)nq_cap[base + i] * pp.G + 2 * BM - 1) / (2 * BM));
       ko += (kv_cap[base + i] + BN - 1) / BN;
     }
     pp.rtile_off[n] = ro;
@@ -693,7 +721,7 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     pp.vt = reinterpret_cast<__half*>(w + pl.q_bytes + pl.k_bytes);
     if (!make_tmap(&pp.tm_q, pp.qp, (int64_t)pp.Hkv * pp.RT * BM, BM) ||
         !make_tmap(&pp.tm_k, pp.kp, (int64_t)pp.Hkv * std::max(pp.KT, 1) * BN, BN) ||
-        !make_tmap(&pp.tm_v, pp.vt, (int64_t)pp.Hkv * std::max(pp.KT, 1) * VROWS, VROWS))
+        !make_tmap(&pp.tm_v, pp.vt, (int64_t)pp.Hkv * std::max(pp.KT, 1) * D, BN))
       return cudaErrorInvalidValue;
     if (pp.KT > 0) {
       pack_kv_kernel<<<dim3(pp.KT, pp.Hkv), 256, 0, stream>>>(pp);
@@ -701,11 +729,11 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     }
     pack_q_kernel<<<dim3(pp.RT, pp.Hkv), 256, 0, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t smem = (size_t)(1 + KST) * TILE_BYTES + (size_t)VST * VTILE_BYTES + 1024;
+    const size_t smem = (size_t)(2 + KST + VST) * TILE_BYTES + 1024;
     auto kern = (p.mask || !(p.scale > 0.f)) ? prefill_kernel<true> : prefill_kernel<false>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
       return e;
-    kern<<<pp.Hkv * pp.RT, NTHREADS, smem, stream>>>(pp);
+    kern<<<pp.Hkv * (pp.RT / 2), NTHREADS, smem, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
   return cudaSuccess;
