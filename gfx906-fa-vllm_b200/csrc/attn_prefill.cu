@@ -300,21 +300,60 @@ constexpr uint32_t kIdesc = (1u << 4)                       // D format f32
 // ===========================================================================
 // attention kernel
 // ===========================================================================
-// 2^x on the FMA pipe for x <= 2^7 (Cody-Waite split into floor and
-// fraction, then a degree-3 minimax polynomial for 2^f on [0, 1), relative
-// error 7.5e-5, below the fp16 rounding of P).  floor(x) comes from adding
-// 1.5 * 2^23 with round-down, which leaves it in the low mantissa bits;
-// shifting those bits into the exponent field scales the polynomial.  Inputs
-// below -126 (including -inf) are clamped to -126: the polynomial lies in
-// [0.99992, 2), so its exponent field stays >= 0 (a denormal at most, which
-// rounds to 0 in fp16) and never borrows into the sign bit.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = __fadd_rd(x, 12582912.f);
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.07802300900220871f, f, 0.2260693907737732f), f, 0.6958328485488892f), f,
-                       0.9999252557754517f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+// Packed fp32 pairs (Blackwell f32x2 arithmetic: one instruction, two lanes).
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2add_rd(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe, for x <= 2^7 (Cody-Waite split into floor
+// and fraction, then a degree-3 minimax polynomial for 2^f on [0, 1),
+// relative error 7.5e-5, below the fp16 rounding of P).  floor(x) comes from
+// adding 1.5 * 2^23 with round-down, which leaves it in the low mantissa
+// bits; shifting those bits into the exponent field scales the polynomial.
+// Inputs below -126 (including -inf) are clamped to -126: the polynomial lies
+// in [0.99992, 2), so its exponent field stays >= 0 (a denormal at most,
+// which rounds to 0 in fp16) and never borrows into the sign bit.
+__device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
+  float a, b;
+  f2unpack(x2, a, b);
+  x2 = f2pack(fmaxf(a, -126.f), fmaxf(b, -126.f));
+  const uint64_t magic = f2pack(12582912.f, 12582912.f);
+  const uint64_t t = f2add_rd(x2, magic);
+  const uint64_t f = f2sub(x2, f2sub(t, magic));
+  uint64_t p = f2fma(f2pack(0.07802300900220871f, 0.07802300900220871f), f,
+                     f2pack(0.2260693907737732f, 0.2260693907737732f));
+  p = f2fma(p, f, f2pack(0.6958328485488892f, 0.6958328485488892f));
+  p = f2fma(p, f, f2pack(0.9999252557754517f, 0.9999252557754517f));
+  float p0, p1, t0, t1;
+  f2unpack(p, p0, p1);
+  f2unpack(t, t0, t1);
+  return f2pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
+                __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
 }
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -556,18 +595,27 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
       // P = 2^(x - m): one pair in four on the FMA pipe, the rest on MUFU
       const float mu = m_run == -INFINITY ? 0.f : m_run;
       const float sc = MASK ? 1.f : pp.scale_log2;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint64_t sc2 = f2pack(sc, sc);
+      const uint64_t nmu2 = f2pack(-mu, -mu);
+      uint64_t ls2[2] = {0ull, 0ull};                     // row-sum pairs (0.0f bit pattern is 0)
 #pragma unroll
       for (int c = 0; c < 8; ++c) {                        // 16 keys -> 8 packed columns
         uint32_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float x0 = fmaf(__uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e]), sc, -mu);
-          const float x1 = fmaf(__uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e + 1]), sc, -mu);
+          const uint64_t x2 = f2fma(f2pack(__uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e]),
+                                           __uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e + 1])), sc2, nmu2);
+          uint64_t p2;
+          if ((e & 3) == 3) {
+            p2 = exp2_fma2(x2);
+          } else {
+            float x0, x1;
+            f2unpack(x2, x0, x1);
+            p2 = f2pack(fast_exp2(x0), fast_exp2(x1));
+          }
+          ls2[e & 1] = f2add(ls2[e & 1], p2);
           float p0, p1;
-          if ((e & 3) == 3) { p0 = exp2_fma(x0); p1 = exp2_fma(x1); }
-          else { p0 = fast_exp2(x0); p1 = fast_exp2(x1); }
-          ls[c & 3] += p0 + p1;
+          f2unpack(p2, p0, p1);
           pk[e] = pack_half2(p0, p1);
         }
         asm volatile(
@@ -576,7 +624,12 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
               "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
             : "memory");
       }
-      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      {
+        float a0, a1, b0, b1;
+        f2unpack(ls2[0], a0, a1);
+        f2unpack(ls2[1], b0, b1);
+        l_run += (a0 + a1) + (b0 + b1);
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar_p[wi]);
