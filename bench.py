@@ -108,8 +108,10 @@ class ClockSampler:
 # workload construction (on the GPU)
 # ---------------------------------------------------------------------------
 def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
-    """Paged Q8_0 K + fp16 V cache for sequences of `lens` tokens, shuffled
-    pages, filled by the fused store kernel from N(0,1) fp16 K/V."""
+    """Paged Q8_0 K + V cache for sequences of `lens` tokens, shuffled pages,
+    filled by the fused store kernel from N(0,1) fp16 K/V.  v_fmt: "fp16",
+    "q8_0" (page-transposed Q8_0 records, the backend's layout) or
+    "q8_0rows" (Q8_0 token rows)."""
     import torch
     import gfx906_fa
     g = torch.Generator(device=device).manual_seed(seed)
@@ -124,6 +126,8 @@ def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
         c += n
     k_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
     if v_fmt == "q8_0":
+        v_cache = torch.zeros((NB, hkv, BS * RB), dtype=torch.uint8, device=device)
+    elif v_fmt == "q8_0rows":
         v_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
     else:
         v_cache = torch.zeros((NB, BS, hkv, D), dtype=torch.float16, device=device)
@@ -135,7 +139,7 @@ def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
             slots = bt[b, tpos // BS].to(torch.int64) * BS + tpos % BS
             k = torch.randn((n, hkv, D), generator=g, device=device, dtype=torch.float16)
             v = torch.randn((n, hkv, D), generator=g, device=device, dtype=torch.float16)
-            gfx906_fa.store_kv(k, v, slots, k_cache, v_cache, 2 if v_fmt == "q8_0" else 1)
+            gfx906_fa.store_kv(k, v, slots, k_cache, v_cache, {"q8_0": 3, "q8_0rows": 2}.get(v_fmt, 1))
     return k_cache, v_cache, bt
 
 
@@ -206,7 +210,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--v-fmt", default="fp16", choices=["fp16", "q8_0"])
+    ap.add_argument("--v-fmt", default="fp16", choices=["fp16", "q8_0", "q8_0rows"])
     ap.add_argument("--decode-seqs", type=int, default=64,
                     help="first N sequences of config 3 (profiling uses a smaller case)")
     ap.add_argument("--prefill-tokens", type=int, default=32768)
@@ -296,7 +300,7 @@ def main():
         barrier()
     total_ms = max_over_ranks(t_start.elapsed_time(t_end))
     per_launch_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
-    v_row = RB if args.v_fmt == "q8_0" else 2 * D
+    v_row = RB if args.v_fmt.startswith("q8_0") else 2 * D
     bytes_rank = decode_bytes(lens, hkv, hq, v_row)
     bytes_all = bytes_rank * world
     ms_per_step = total_ms / args.steps
@@ -386,7 +390,8 @@ def main():
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 Q / q8_0 K / "
-            + ("q8_0" if args.v_fmt == "q8_0" else "fp16") + " V, fp32 accumulate",
+            + {"q8_0": "q8_0 (page-transposed)", "q8_0rows": "q8_0 rows"}.get(args.v_fmt, "fp16")
+            + " V, fp32 accumulate",
             "data": "synthetic",
             "config": {"workload": f"config3 decode: {B} seqs x 1 query, L~U[1K,32K] seed 3, GQA 48/8, d128, "
                                    "block 16, shuffled pages",

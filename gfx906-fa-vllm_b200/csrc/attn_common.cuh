@@ -43,8 +43,10 @@ __device__ __forceinline__ void store_out2(void* out, int dt, int64_t off, float
 // ---------------------------------------------------------------------------
 // warp-level tensor-core MMA (m16n8k16, 16-bit inputs, fp32 accumulators)
 // ---------------------------------------------------------------------------
+// Register-only: not volatile, so the compiler may schedule shared-memory
+// loads for later fragments ahead of it.
 __device__ __forceinline__ void mma_f16_16816(float c[4], const uint32_t a[4], const uint32_t b[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -52,11 +54,26 @@ __device__ __forceinline__ void mma_f16_16816(float c[4], const uint32_t a[4], c
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float c[4], const uint32_t a[4], const uint32_t b[2]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// Four 8x8 b16 matrices; thread l gets, of each matrix, the 4 bytes at
+// columns 2*(l%4), 2*(l%4)+1 of row l/4.  Lanes 8m..8m+7 supply the row
+// addresses of matrix m (16-byte aligned rows).
+__device__ __forceinline__ void ldmatrix_x4(uint32_t r[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint2 lds_u64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
 }
 
 __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t r[4], uint32_t addr) {

@@ -51,6 +51,7 @@ constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, 
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*232 + 128*40
 constexpr int REG_COMPUTE = 232;
 constexpr int REG_PRODUCER = 40;
+constexpr float kRescaleLog2 = 8.0f;        // lazy-max threshold (log2 units): P <= 2^8
 }  // namespace dec
 
 struct DecodeParams {
@@ -64,6 +65,8 @@ struct DecodeParams {
   int n_items;
   int R_pad;              // 16 * MT
   int rb_k, rb_v;         // bytes of one K / V row
+  int vrec;               // page-transposed Q8_0 V: bytes of one (page, head) record
+  int vrec_contig;        // 1: the records of a CTA's kv heads are adjacent (one copy per page)
   int kgs, vgs;           // smem bytes per K group (4 tokens) / V group (2 tokens), padded to odd x 16
   int contig;             // 1: rows of consecutive tokens are adjacent (one copy per group)
   int kpage, vpage;       // smem bytes per page
@@ -110,7 +113,8 @@ __device__ __forceinline__ void named_sync_compute() {
   asm volatile("bar.sync 1, %0;" ::"n"(dec::NWC * 32) : "memory");
 }
 
-// MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0).
+// MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0 rows,
+// 3 Q8_0 page-transposed records).
 // NST: shared-memory pipeline slots.
 template <int MT, int VT, bool MASK, int NST>
 __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodeParams d) {
@@ -198,6 +202,16 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           const int nkc = d.contig ? 4 : 16;
           const bool isk = r < nkc;
           const int q = isk ? r : r - nkc;
+          if constexpr (VT == 3) {
+            if (!isk) {
+              // one copy of the adjacent records of all HG heads, or one per head
+              if (q >= (d.vrec_contig ? 1 : d.HG)) continue;
+              bulk_g2s(vdst0 + j * d.vpage + q * d.vrec,
+                       p.v_cache + (int64_t)phys_j * p.v_page_stride + (int64_t)(h0 + q) * p.v_head_stride,
+                       d.vrec_contig ? d.HG * d.vrec : d.vrec, &full_bar[slot]);
+              continue;
+            }
+          }
           if (!isk && q >= (d.contig ? 8 : 16)) continue;
           const int hgb = isk ? hgb_k : hgb_v;
           const int gt = isk ? 4 : 2;             // tokens per group
@@ -258,6 +272,12 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   };
 
   const uint32_t smem_base = smem_u32(smem);
+  // shared-memory loads as plain C++ loads through the __shared__ array (the
+  // compiler folds constant offsets and schedules them; the "memory" clobber
+  // of the mbarrier waits keeps them after the data has landed)
+  auto ld16 = [&](uint32_t a) { return *reinterpret_cast<const uint16_t*>(smem + (a - smem_base)); };
+  auto ld8 = [&](uint32_t a) { return (uint32_t)*reinterpret_cast<const uint8_t*>(smem + (a - smem_base)); };
+  auto ld64 = [&](uint32_t a) { return *reinterpret_cast<const uint2*>(smem + (a - smem_base)); };
   const uint32_t qs_base = smem_base + d.q_off + hl * (MT * 16 * QROW);
 
   auto load_q = [&](int b, int h) {
@@ -482,12 +502,12 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t qb = krow + blk * QBLOCK + 2 + 2 * j4;
           uint32_t b0[2], b1[2];
-          b0[0] = i8x2_to_h2(lds_u16(qb));
-          b0[1] = i8x2_to_h2(lds_u16(qb + 8));
-          b1[0] = i8x2_to_h2(lds_u16(qb + 16));
-          b1[1] = i8x2_to_h2(lds_u16(qb + 24));
-          const float dk0 = half_bits_to_float(lds_u16(kcol0 + blk * QBLOCK));
-          const float dk1 = half_bits_to_float(lds_u16(kcol1 + blk * QBLOCK));
+          b0[0] = i8x2_to_h2(ld16(qb));
+          b0[1] = i8x2_to_h2(ld16(qb + 8));
+          b1[0] = i8x2_to_h2(ld16(qb + 16));
+          b1[1] = i8x2_to_h2(ld16(qb + 24));
+          const float dk0 = half_bits_to_float(ld16(kcol0 + blk * QBLOCK));
+          const float dk1 = half_bits_to_float(ld16(kcol1 + blk * QBLOCK));
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -506,10 +526,14 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
       // ---------------- mask + online softmax (base 2) ------------------------
       // pages every row sees completely need no per-element mask
       const bool page_full = !MASK && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1);
+      // Lazy running max: a row keeps its reference max m until one of its
+      // scores exceeds m by more than 2^8; only then (rare after the first
+      // pages) is the row max reduced over the quad and O / l rescaled.  So
+      // P <= 2^8, and the usual page needs no shuffles and no rescale.
       uint32_t pa[MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        float alpha2[2];
+        float tmx[2];
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int r = mt * 16 + rq + hh * 8;
@@ -535,13 +559,34 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
               sacc[mt][nt][hh * 2 + c] = x;
               mx = fmaxf(mx, x);
             }
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float mn = fmaxf(mrow[mt][hh], mx);
-          const float mu = mn == -INFINITY ? 0.f : mn;
-          const float alpha = fast_exp2(mrow[mt][hh] - mu);
-          alpha2[hh] = alpha;
-          mrow[mt][hh] = mn;
+          tmx[hh] = mx;
+        }
+        const bool grow = tmx[0] > mrow[mt][0] + kRescaleLog2 || tmx[1] > mrow[mt][1] + kRescaleLog2;
+        if (__any_sync(0xffffffffu, grow)) {
+          float alpha2[2];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            float mx = tmx[hh];
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+            alpha2[hh] = 1.f;
+            if (mx > mrow[mt][hh] + kRescaleLog2) {              // uniform over the quad
+              alpha2[hh] = fast_exp2(mrow[mt][hh] - mx);          // 0 for the first visible key
+              mrow[mt][hh] = mx;
+              lrow[mt][hh] *= alpha2[hh];
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < 16; ++nt) {
+            o[mt][nt][0] *= alpha2[0];
+            o[mt][nt][1] *= alpha2[0];
+            o[mt][nt][2] *= alpha2[1];
+            o[mt][nt][3] *= alpha2[1];
+          }
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float mu = mrow[mt][hh] == -INFINITY ? 0.f : mrow[mt][hh];
           float ls = 0.f;
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
@@ -551,18 +596,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
               sacc[mt][nt][hh * 2 + c] = pv;
               ls += pv;
             }
-          lrow[mt][hh] = lrow[mt][hh] * alpha + ls;
-        }
-        // the running max rarely grows after the first pages: skip the O
-        // rescale when no row of the warp changed
-        if (__any_sync(0xffffffffu, alpha2[0] != 1.f || alpha2[1] != 1.f)) {
-#pragma unroll
-          for (int nt = 0; nt < 16; ++nt) {
-            o[mt][nt][0] *= alpha2[0];
-            o[mt][nt][1] *= alpha2[0];
-            o[mt][nt][2] *= alpha2[1];
-            o[mt][nt][3] *= alpha2[1];
-          }
+          lrow[mt][hh] += ls;
         }
         if constexpr (VT == 1) {
           pa[mt][0] = pack_bf162(sacc[mt][0][0], sacc[mt][0][1]);
@@ -577,7 +611,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         }
       }
       // ---------------- O += P V ------------------------------------------------
-      if constexpr (VT != 2) {
+      if constexpr (VT < 2) {
         // ldmatrix.trans: thread i addresses matrix i/8 row i%8; matrices
         // (keys 0-7 | 8-15) x (d block nt | nt+1)
         const int mi = lane >> 3, ri = lane & 7;
@@ -599,6 +633,36 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             }
           }
         }
+      } else if constexpr (VT == 3) {
+        // Page-transposed Q8_0 V: dim rows of 16 keys.  ldmatrix hands each
+        // thread the 4 bytes of keys 4*j4 .. 4*j4+3 of dim nt*8 + rq; the
+        // B fragment wants k-slots (2*j4, 2*j4+1) = keys (4*j4, 4*j4+3) and
+        // (2*j4+8, 2*j4+9) = keys (4*j4+1, 4*j4+2) (the key order above), so
+        // a byte permute builds each pair.  int8 -> fp16 is exact
+        // ((0x6400 | (b ^ 0x80)) - 1152); the scale is applied in fp16.
+        const uint32_t vrec = smem_base + slot * d.stage_bytes + d.P * d.kpage + sub * d.vpage + hl * d.vrec;
+        const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          uint32_t r4[4];
+          ldmatrix_x4(r4, vrec + 2 * 4 * PAGE + (blk * 32 + lane) * PAGE);
+          const uint2 sc = ld64(vrec + blk * 2 * PAGE + 8 * j4);
+          const uint32_t s03u = __byte_perm(sc.x, sc.y, 0x7610);
+          const uint32_t s12u = __byte_perm(sc.x, sc.y, 0x5432);
+          const __half2 s03 = *reinterpret_cast<const __half2*>(&s03u);
+          const __half2 s12 = *reinterpret_cast<const __half2*>(&s12u);
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const uint32_t w = r4[m] ^ 0x80808080u;
+            uint32_t t0 = __byte_perm(w, 0x64646464u, 0x4340);
+            uint32_t t1 = __byte_perm(w, 0x64646464u, 0x4241);
+            const __half2 x0 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&t0), bias), s03);
+            const __half2 x1 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&t1), bias), s12);
+            const uint32_t bq[2] = {*reinterpret_cast<const uint32_t*>(&x0), *reinterpret_cast<const uint32_t*>(&x1)};
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][blk * 4 + m], pa[mt], bq);
+          }
+        }
       } else {
         // V rows are Q8_0: B fragment element (key k, dim n) = q8[k][n] * d[k][n/32]
         // k-slots 2j, 2j+1, 2j+8, 2j+9
@@ -609,17 +673,13 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t so = blk * QBLOCK;
-          const __half2 s01 = __halves2half2(__ushort_as_half(lds_u16(r0 + so)), __ushort_as_half(lds_u16(r1 + so)));
-          const __half2 s89 = __halves2half2(__ushort_as_half(lds_u16(r8 + so)), __ushort_as_half(lds_u16(r9 + so)));
+          const __half2 s01 = __halves2half2(__ushort_as_half(ld16(r0 + so)), __ushort_as_half(ld16(r1 + so)));
+          const __half2 s89 = __halves2half2(__ushort_as_half(ld16(r8 + so)), __ushort_as_half(ld16(r9 + so)));
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int nt = blk * 4 + q;
             const uint32_t off = so + 2 + q * 8 + rq;          // dim n = nt*8 + rq
-            uint32_t v0, v1, v8, v9;
-            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v0) : "r"(r0 + off));
-            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v1) : "r"(r1 + off));
-            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v8) : "r"(r8 + off));
-            asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v9) : "r"(r9 + off));
+            const uint32_t v0 = ld8(r0 + off), v1 = ld8(r1 + off), v8 = ld8(r8 + off), v9 = ld8(r9 + off);
             uint32_t h01 = i8x2_to_h2(v0 | (v1 << 8));
             uint32_t h89 = i8x2_to_h2(v8 | (v9 << 8));
             __half2 x01 = __hmul2(*reinterpret_cast<__half2*>(&h01), s01);
@@ -697,7 +757,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   if (p.num_seqs < 0 || p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv)
     return cudaErrorInvalidValue;
   if (p.seq_q < 0 || p.max_kv < 0 || p.max_blocks < 0) return cudaErrorInvalidValue;
-  if (p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2 || p.v_fmt < 0 || p.v_fmt > 2)
+  if (p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2 || p.v_fmt < 0 || p.v_fmt > 3)
     return cudaErrorInvalidValue;
   d = DecodeParams{};
   d.p = p;
@@ -712,29 +772,37 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   d.HGN = Hkv / d.HG;
   d.P = NWC / d.HG;
   d.rb_k = q8_row_bytes(D);
-  d.rb_v = p.v_fmt == G9_VFMT_Q8 ? q8_row_bytes(D) : 2 * D;
+  const bool vq8t = p.v_fmt == G9_VFMT_Q8T;
+  d.rb_v = (p.v_fmt == G9_VFMT_Q8 || vq8t) ? q8_row_bytes(D) : 2 * D;
   // dense pages: the rows of one token (all heads) are contiguous
   if (p.k_head_stride != d.rb_k || p.k_tok_stride != (int64_t)Hkv * d.rb_k) return cudaErrorInvalidValue;
-  if (p.v_head_stride != d.rb_v || p.v_tok_stride != (int64_t)Hkv * d.rb_v) return cudaErrorInvalidValue;
+  if (!vq8t && (p.v_head_stride != d.rb_v || p.v_tok_stride != (int64_t)Hkv * d.rb_v)) return cudaErrorInvalidValue;
+  d.vrec = PAGE * d.rb_v;                 // page-transposed record (2176 bytes)
+  if (vq8t && (p.v_head_stride < d.vrec || p.v_head_stride % 16)) return cudaErrorInvalidValue;
+  d.vrec_contig = vq8t && p.v_head_stride == d.vrec;
   // Shared-memory layout per page: K in 4 groups of 4 tokens, V in 8 groups of
   // 2 tokens, each group padded to an odd multiple of 16 bytes.  When the
   // row groups of consecutive tokens are adjacent in HBM (all kv heads in one
   // CTA) a group is one bulk copy, else one copy per token.  Copies need
   // 16-byte aligned sources and sizes.
   const int hgk = d.HG * d.rb_k, hgv = d.HG * d.rb_v;
-  d.contig = p.k_tok_stride == hgk && p.v_tok_stride == hgv;
+  d.contig = p.k_tok_stride == hgk && (vq8t || p.v_tok_stride == hgv);
   if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.v_page_stride) & 15)
     return cudaErrorInvalidValue;
-  if (((int64_t)d.HG * p.k_head_stride) % 16 || ((int64_t)d.HG * p.v_head_stride) % 16) return cudaErrorInvalidValue;
+  if (((int64_t)d.HG * p.k_head_stride) % 16 || (!vq8t && ((int64_t)d.HG * p.v_head_stride) % 16))
+    return cudaErrorInvalidValue;
   if (d.contig) {
-    if ((2 * hgk) % 16 || (2 * hgv) % 16) return cudaErrorInvalidValue;
+    if ((2 * hgk) % 16 || (!vq8t && (2 * hgv) % 16)) return cudaErrorInvalidValue;
   } else {
-    if (hgk % 16 || hgv % 16 || p.k_tok_stride % 16 || p.v_tok_stride % 16) return cudaErrorInvalidValue;
+    if (hgk % 16 || p.k_tok_stride % 16) return cudaErrorInvalidValue;
+    if (!vq8t && (hgv % 16 || p.v_tok_stride % 16)) return cudaErrorInvalidValue;
   }
   d.kgs = pad_odd16(4 * hgk);
   d.vgs = pad_odd16(2 * hgv);
   d.kpage = (PAGE / 4) * d.kgs;
-  d.vpage = (PAGE / 2) * d.vgs;
+  // page-transposed V: the HG records back to back (ldmatrix rows are 16
+  // consecutive bytes, conflict-free at any 16-byte aligned base)
+  d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
   d.stage_bytes = d.P * (d.kpage + d.vpage);
   const int wph = NWC / d.HG;
   const int merge_bytes = wph > 1 ? d.HG * mt * (16 * 4 + 4) * 32 * 4 : 0;
@@ -819,9 +887,9 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
 #define G9_DEC(MT_, VT_, MK_) \
   if (mt == MT_ && vt == VT_ && mask == MK_) return launch_decode_t<MT_, VT_, MK_>(d, stream);
   G9_DEC(1, 0, false) G9_DEC(2, 0, false) G9_DEC(1, 1, false) G9_DEC(2, 1, false)
-  G9_DEC(1, 2, false) G9_DEC(2, 2, false)
+  G9_DEC(1, 2, false) G9_DEC(2, 2, false) G9_DEC(1, 3, false) G9_DEC(2, 3, false)
   G9_DEC(1, 0, true) G9_DEC(2, 0, true) G9_DEC(1, 1, true) G9_DEC(2, 1, true)
-  G9_DEC(1, 2, true) G9_DEC(2, 2, true)
+  G9_DEC(1, 2, true) G9_DEC(2, 2, true) G9_DEC(1, 3, true) G9_DEC(2, 3, true)
 #undef G9_DEC
   return cudaErrorInvalidValue;
 }

@@ -128,7 +128,17 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
       }
       const uint8_t* vrow = p.v_cache + (int64_t)max(phys, 0) * p.v_page_stride + off_t * p.v_tok_stride +
                             (int64_t)h * p.v_head_stride;
-      if (p.v_fmt == G9_VFMT_Q8) {
+      if (p.v_fmt == G9_VFMT_Q8T) {
+        // page-transposed record: scale (block j, token t) at 2*(j*bs + t),
+        // int8 (dim, token t) at 2*(D/32)*bs + dim*bs + t
+        const uint8_t* rec = p.v_cache + (int64_t)max(phys, 0) * p.v_page_stride + (int64_t)h * p.v_head_stride;
+        const int bsz = p.block_size;
+        const float dv = __half2float(__ushort_as_half(
+            *reinterpret_cast<const uint16_t*>(rec + 2 * ((int64_t)(c >> 1) * bsz + off_t))));
+        const int8_t* vq = reinterpret_cast<const int8_t*>(rec + 2 * (D / QK) * bsz + off_t) + (int64_t)(c * 16) * bsz;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) vv[e] = __float2half_rn((float)vq[(int64_t)e * bsz] * dv);
+      } else if (p.v_fmt == G9_VFMT_Q8) {
         const uint8_t* vb = vrow + (c >> 1) * QBLOCK;
         const float dv = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(vb)));
         const uint16_t* vq = reinterpret_cast<const uint16_t*>(vb + 2 + (c & 1) * 16);
@@ -728,11 +738,11 @@ static cudaError_t check_prefill_batch(const G9AttnBatch& p) {
   if (p.head_dim != pf::D) return cudaErrorInvalidValue;
   if (p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv) return cudaErrorInvalidValue;
   if (p.block_size <= 0 || p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2) return cudaErrorInvalidValue;
-  if (p.v_fmt < 0 || p.v_fmt > 2) return cudaErrorInvalidValue;
+  if (p.v_fmt < 0 || p.v_fmt > 3) return cudaErrorInvalidValue;
   // K rows and Q8_0 V rows are read with 2-byte loads, 16-bit V rows with 4-byte loads
   if (((uintptr_t)p.k_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.k_tok_stride | (uintptr_t)p.k_head_stride) & 1)
     return cudaErrorInvalidValue;
-  const uintptr_t va = p.v_fmt == G9_VFMT_Q8 ? 1 : 3;
+  const uintptr_t va = (p.v_fmt == G9_VFMT_Q8 || p.v_fmt == G9_VFMT_Q8T) ? 1 : 3;
   if (((uintptr_t)p.v_cache | (uintptr_t)p.v_page_stride | (uintptr_t)p.v_tok_stride | (uintptr_t)p.v_head_stride) & va)
     return cudaErrorInvalidValue;
   return cudaSuccess;

@@ -37,7 +37,7 @@ struct StoreArgs {
   int64_t kc_blk, kc_tok, kc_head;  // bytes
   int64_t vc_blk, vc_tok, vc_head;  // bytes
   int key_dt, val_dt;
-  int v_mode;                   // 0: no V, 1: copy 16-bit rows, 2: quantise to Q8_0
+  int v_mode;                   // 0: no V, 1: copy 16-bit rows, 2: Q8_0 rows, 3: Q8_0 page-transposed
   int T, Hkv, D, bs;
   int k_store_w;                // widest aligned store for K rows (2, 4 or 8 bytes)
   int v_store_w;                // same for V rows
@@ -133,6 +133,20 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_kernel(StoreArgs a) {
                          a.vec_ok_v, stage);
       stage_to_global(stage, a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head, rb,
                       a.v_store_w);
+    } else if (a.v_mode == 3) {
+      // page-transposed record of (page, head): fp16 scales [D/32][bs], then
+      // int8 values [D][bs]
+      quant_row_to_stage(a.value, (int64_t)t * a.val_tok + (int64_t)h * a.val_head, a.val_dt, a.D,
+                         a.vec_ok_v, stage);
+      uint8_t* rec = a.v_cache + blk * a.vc_blk + h * a.vc_head;
+      const int nb = a.D / QK;
+      const int lane = lane_id();
+      for (int j = lane; j < nb; j += 32)
+        *reinterpret_cast<uint16_t*>(rec + 2 * ((int64_t)j * a.bs + off)) =
+            *reinterpret_cast<const uint16_t*>(stage + j * QBLOCK);
+      uint8_t* qv = rec + 2 * nb * a.bs + off;
+      for (int i = lane; i < a.D; i += 32) qv[(int64_t)i * a.bs] = stage[(i / QK) * QBLOCK + 2 + (i % QK)];
+      __syncwarp();
     } else if (a.v_mode == 1) {
       const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) +
                             (int64_t)t * a.val_tok + (int64_t)h * a.val_head;
@@ -224,7 +238,9 @@ extern "C" cudaError_t gfx906_fa_store_kv(
   if (head_size % QK != 0 || head_size <= 0 || head_size > kMaxD) return cudaErrorInvalidValue;
   if (num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0) return cudaErrorInvalidValue;
   if (key_dtype < 0 || key_dtype > 2) return cudaErrorInvalidValue;
-  if (v_mode < 0 || v_mode > 2) return cudaErrorInvalidValue;
+  if (v_mode < 0 || v_mode > 3) return cudaErrorInvalidValue;
+  if (v_mode == G9_V_Q8T && (((uintptr_t)v_cache | (uintptr_t)v_block_stride | (uintptr_t)v_head_stride) & 1))
+    return cudaErrorInvalidValue;                   // fp16 scales are written with 2-byte stores
   if (v_mode == G9_V_COPY16 && value_dtype == G9_DT_F32) return cudaErrorInvalidValue;
   if (v_mode != G9_V_NONE && (value == nullptr || v_cache == nullptr)) return cudaErrorInvalidValue;
   if (num_tokens == 0) return cudaSuccess;
@@ -239,7 +255,7 @@ extern "C" cudaError_t gfx906_fa_store_kv(
   a.T = num_tokens; a.Hkv = num_kv_heads; a.D = head_size; a.bs = block_size;
   a.k_store_w = store_width(k_cache, k_block_stride, k_token_stride, k_head_stride, rb);
   a.vec_ok_k = vec_aligned(key, key_dtype, key_token_stride, key_head_stride);
-  if (v_mode == G9_V_Q8) {
+  if (v_mode == G9_V_Q8 || v_mode == G9_V_Q8T) {
     a.v_store_w = store_width(v_cache, v_block_stride, v_token_stride, v_head_stride, rb);
     a.vec_ok_v = vec_aligned(value, value_dtype, value_token_stride, value_head_stride);
   } else if (v_mode == G9_V_COPY16) {

@@ -155,7 +155,8 @@ void store_kv(torch::Tensor key, torch::Tensor value, torch::Tensor slot_mapping
   TORCH_CHECK(key.dim() == 3 && key.stride(2) == 1, "key must be [T, Hkv, D] with contiguous D");
   TORCH_CHECK(slot_mapping.dtype() == torch::kInt64 && slot_mapping.dim() == 1, "slot_mapping must be int64 [T]");
   CHECK_CONTIG(slot_mapping);
-  TORCH_CHECK(v_mode >= 0 && v_mode <= 2, "v_mode must be 0 (none), 1 (copy) or 2 (q8_0)");
+  TORCH_CHECK(v_mode >= 0 && v_mode <= 3,
+              "v_mode must be 0 (none), 1 (copy), 2 (q8_0 rows) or 3 (q8_0 page-transposed)");
   const int T = key.size(0), Hkv = key.size(1), D = key.size(2);
   TORCH_CHECK(slot_mapping.size(0) == T, "slot_mapping length mismatch");
   // k_cache / v_cache: 4-D [NB, bs, Hkv, row] views (any dtype) with byte strides
@@ -173,15 +174,23 @@ void store_kv(torch::Tensor key, torch::Tensor value, torch::Tensor slot_mapping
     TORCH_CHECK(value.dim() == 3 && value.size(0) == T && value.size(1) == Hkv && value.size(2) == D &&
                     value.stride(2) == 1,
                 "value must be [T, Hkv, D] with contiguous D");
-    TORCH_CHECK(v_cache.dim() == 4 && v_cache.size(1) == bs && v_cache.size(2) == Hkv,
-                "v_cache must be [NB, bs, Hkv, row]");
     vptr = value.data_ptr();
     vts = value.stride(0);
     vhs = value.stride(1);
     const int64_t ve = v_cache.element_size();
-    vb0 = v_cache.stride(0) * ve;
-    vb1 = v_cache.stride(1) * ve;
-    vb2 = v_cache.stride(2) * ve;
+    if (v_mode == G9_V_Q8T) {
+      TORCH_CHECK(v_cache.dim() == 3 && v_cache.size(1) == Hkv && v_cache.dtype() == torch::kUInt8 &&
+                      v_cache.size(2) == (int64_t)bs * (D / 32) * 34 && v_cache.stride(2) == 1,
+                  "v_cache must be uint8 [NB, Hkv, block_size*(D/32)*34] page-transposed records");
+      vb0 = v_cache.stride(0);
+      vb2 = v_cache.stride(1);
+    } else {
+      TORCH_CHECK(v_cache.dim() == 4 && v_cache.size(1) == bs && v_cache.size(2) == Hkv,
+                  "v_cache must be [NB, bs, Hkv, row]");
+      vb0 = v_cache.stride(0) * ve;
+      vb1 = v_cache.stride(1) * ve;
+      vb2 = v_cache.stride(2) * ve;
+    }
     vc = reinterpret_cast<uint8_t*>(v_cache.data_ptr());
   }
   c10::cuda::CUDAGuard g(key.device());
@@ -205,9 +214,15 @@ G9AttnBatch batch_base(const torch::Tensor& key_cache_q8, const torch::Tensor& v
   b.k_tok_stride = key_cache_q8.stride(1) * ke;
   b.k_head_stride = key_cache_q8.stride(2) * ke;
   b.v_cache = reinterpret_cast<const uint8_t*>(value_cache.data_ptr());
-  b.v_page_stride = value_cache.stride(0) * ve;
-  b.v_tok_stride = value_cache.stride(1) * ve;
-  b.v_head_stride = value_cache.stride(2) * ve;
+  if (v_fmt == G9_VFMT_Q8T) {           // [NB, Hkv, record] uint8
+    b.v_page_stride = value_cache.stride(0);
+    b.v_tok_stride = 0;
+    b.v_head_stride = value_cache.stride(1);
+  } else {
+    b.v_page_stride = value_cache.stride(0) * ve;
+    b.v_tok_stride = value_cache.stride(1) * ve;
+    b.v_head_stride = value_cache.stride(2) * ve;
+  }
   b.v_fmt = v_fmt;
   b.block_table = block_table.data_ptr<int32_t>();
   b.max_blocks = block_table.size(1);
@@ -218,7 +233,13 @@ G9AttnBatch batch_base(const torch::Tensor& key_cache_q8, const torch::Tensor& v
   return b;
 }
 
+// 4-D caches hold token rows; a 3-D uint8 [NB, Hkv, record] cache holds
+// page-transposed Q8_0 records (G9_VFMT_Q8T).
 int infer_v_fmt(const torch::Tensor& value_cache, int64_t D) {
+  if (value_cache.dim() == 3) {
+    TORCH_CHECK(value_cache.dtype() == torch::kUInt8, "a 3-D value_cache must be uint8 page-transposed Q8_0");
+    return G9_VFMT_Q8T;
+  }
   if (value_cache.dtype() == torch::kUInt8) {
     TORCH_CHECK(value_cache.size(3) == (D / 32) * 34, "Q8_0 value_cache last dim must be (D/32)*34");
     return G9_VFMT_Q8;
@@ -239,13 +260,20 @@ void check_paged(const torch::Tensor& key_cache_q8, const torch::Tensor& value_c
   TORCH_CHECK(block_table.dtype() == torch::kInt32, "block_table must be int32");
   TORCH_CHECK(seq_lens.dtype() == torch::kInt32, "seq_lens must be int32");
   TORCH_CHECK(key_cache_q8.dim() == 4, "key_cache_q8 must be [num_blocks, block_size, Hkv, bytes_per_row]");
-  TORCH_CHECK(value_cache.dim() == 4, "value_cache must be [num_blocks, block_size, Hkv, D]");
   TORCH_CHECK(D == 128, "head_dim must be 128");
   TORCH_CHECK(key_cache_q8.size(3) == (D / 32) * 34, "bytes_per_row must equal (D/32)*34");
   TORCH_CHECK(value_cache.size(0) == key_cache_q8.size(0), "value_cache blocks mismatch");
-  TORCH_CHECK(value_cache.size(1) == key_cache_q8.size(1), "value_cache block_size mismatch");
-  TORCH_CHECK(value_cache.size(2) == key_cache_q8.size(2), "value_cache Hkv mismatch");
-  TORCH_CHECK(key_cache_q8.stride(3) == 1 && value_cache.stride(3) == 1, "cache rows must be contiguous");
+  if (value_cache.dim() == 3) {
+    TORCH_CHECK(value_cache.size(1) == key_cache_q8.size(2), "value_cache Hkv mismatch");
+    TORCH_CHECK(value_cache.size(2) == key_cache_q8.size(1) * key_cache_q8.size(3) && value_cache.stride(2) == 1,
+                "page-transposed value_cache must be [num_blocks, Hkv, block_size*(D/32)*34]");
+  } else {
+    TORCH_CHECK(value_cache.dim() == 4, "value_cache must be [num_blocks, block_size, Hkv, D]");
+    TORCH_CHECK(value_cache.size(1) == key_cache_q8.size(1), "value_cache block_size mismatch");
+    TORCH_CHECK(value_cache.size(2) == key_cache_q8.size(2), "value_cache Hkv mismatch");
+    TORCH_CHECK(value_cache.stride(3) == 1, "cache rows must be contiguous");
+  }
+  TORCH_CHECK(key_cache_q8.stride(3) == 1, "cache rows must be contiguous");
   TORCH_CHECK(block_table.dim() == 2 && block_table.size(0) == B, "block_table[0] must equal batch");
   TORCH_CHECK(seq_lens.dim() == 1 && seq_lens.size(0) == B, "seq_lens must be [batch]");
   TORCH_CHECK(block_table.is_contiguous() && seq_lens.is_contiguous(), "block_table / seq_lens must be contiguous");

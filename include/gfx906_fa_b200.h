@@ -33,7 +33,8 @@ extern "C" {
 /* V handling of gfx906_fa_store_kv */
 #define G9_V_NONE 0   /* K only */
 #define G9_V_COPY16 1 /* V copied as 16-bit rows (fp16 / bf16) */
-#define G9_V_Q8 2     /* V quantised to Q8_0 like K */
+#define G9_V_Q8 2     /* V quantised to Q8_0 like K, token rows */
+#define G9_V_Q8T 3    /* V quantised to Q8_0, page-transposed records (G9_VFMT_Q8T) */
 
 /* ======================================================================= */
 /* Reference launchers (same names and argument meaning)                    */
@@ -81,8 +82,10 @@ cudaError_t gfx906_fa_quantize_q8_0(const void* x, int x_dtype, uint8_t* y, int6
                                     cudaStream_t stream);
 
 /* Fused KV store: K [T, Hkv, D] quantised to Q8_0 into k_cache and, per
- * v_mode, V [T, Hkv, D] copied (G9_V_COPY16) or quantised (G9_V_Q8) into
- * v_cache, both addressed by slot_mapping (slot < 0 skips the token).
+ * v_mode, V [T, Hkv, D] copied (G9_V_COPY16) or quantised (G9_V_Q8 token
+ * rows, G9_V_Q8T page-transposed records; v_token_stride is ignored for the
+ * latter) into v_cache, both addressed by slot_mapping (slot < 0 skips the
+ * token).
  * Element strides for key/value, byte strides for the caches.  Replaces the
  * pair vLLM triton_reshape_and_cache_flash + reshape_and_cache_q8 called by
  * Gfx906FAImpl.do_kv_cache_update (extension/gfx906_fa_backend.py:405-442). */
@@ -103,6 +106,17 @@ cudaError_t gfx906_fa_store_kv(const void* key, int key_dtype, int64_t key_token
 #define G9_VFMT_F16 0
 #define G9_VFMT_BF16 1
 #define G9_VFMT_Q8 2
+/* Q8_0 V, page-transposed: the Q8_0 blocks of V (the same int8 values and
+ * fp16 scales as G9_VFMT_Q8) are stored per (page, kv head) as one record of
+ * block_size*(head_dim/32)*34 bytes at page*v_page_stride + h*v_head_stride:
+ *   bytes [0, 2*(head_dim/32)*block_size): fp16 scale of block j of token t
+ *                                           at 2*(j*block_size + t)
+ *   then head_dim rows of block_size int8: value of dim d of token t at
+ *        2*(head_dim/32)*block_size + d*block_size + t
+ * so that the tensor cores read the keys of one dim as consecutive bytes.
+ * v_tok_stride is ignored.  No reference counterpart (the reference keeps V
+ * in fp16). */
+#define G9_VFMT_Q8T 3
 
 /* One attention call.  All pointers are device pointers.
  *
@@ -117,7 +131,7 @@ cudaError_t gfx906_fa_store_kv(const void* key, int key_dtype, int64_t key_token
  * block_table[b*max_blocks + k/block_size] at
  *   page*page_stride + (k%block_size)*tok_stride + h*head_stride   (bytes).
  * K rows are Q8_0 (head_dim/32*34 bytes); V rows are fp16 / bf16 or Q8_0
- * (v_fmt).  max_kv is a host-side upper bound of kv_len.
+ * (v_fmt), or Q8_0 page-transposed records (G9_VFMT_Q8T, above).  max_kv is a host-side upper bound of kv_len.
  *
  * Visibility: key k is visible to query token t iff k < kv_len[b] and, when
  * q_abs != NULL, k <= q_abs[b] + t (the reference's inline causal rule,

@@ -103,6 +103,27 @@ def reshape_and_cache(key: np.ndarray, slot_mapping: np.ndarray, k_cache: np.nda
                                 _i64(Hkv * rb), _i64(rb))
 
 
+def store_v_q8t(value: np.ndarray, slot_mapping: np.ndarray, v_cache: np.ndarray, bs: int,
+                dtype: str | None = None) -> None:
+    """In-place store of V into page-transposed Q8_0 records v_cache
+    [NB, Hkv, bs*D/32*34] (this build's V layout; no reference counterpart).
+    The Q8_0 blocks are those of quantize_q8_0(value) -- scale of block j of
+    token t at bytes 2*(j*bs + t), int8 of dim d at 2*(D/32)*bs + d*bs + t."""
+    T, Hkv, D = value.shape
+    nb = D // QK
+    rows = quantize_q8_0(value, dtype).reshape(T, Hkv, nb, BLOCK_BYTES)
+    for t in range(T):
+        s = int(slot_mapping[t])
+        if s < 0:
+            continue
+        page, off = divmod(s, bs)
+        for h in range(Hkv):
+            rec = v_cache[page, h]
+            for j in range(nb):
+                rec[2 * (j * bs + off):2 * (j * bs + off) + 2] = rows[t, h, j, :2]
+                rec[2 * nb * bs + (j * QK) * bs + off:2 * nb * bs + (j * QK + QK) * bs + off:bs] = rows[t, h, j, 2:]
+
+
 def store_v16(value: np.ndarray, slot_mapping: np.ndarray, v_cache: np.ndarray) -> None:
     """In-place fp16/bf16 copy of V rows by slot (vLLM's reshape_and_cache for V)."""
     value = np.ascontiguousarray(value)
@@ -169,9 +190,11 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
     k_cache [NB, bs, Hkv, D/32*34] u8; v_cache [NB, bs, Hkv, D] fp16 (or q8
     bytes when v_q8).  Strides (seq, tok, head) are in elements for q/out and
     (page, tok, head) in bytes for the caches.  bs: tokens per page (default
-    k_cache.shape[1]); v_fmt: "f16" (default), "bf16" or "q8" (= v_q8).
+    k_cache.shape[1]); v_fmt: "f16" (default), "bf16", "q8" (= v_q8) or "q8t"
+    (page-transposed Q8_0 records, v_cache [NB, Hkv, bs*D/32*34], v_strides
+    (page, unused, head)).
     """
-    vcode = {"f16": 0, "bf16": 1, "q8": 2}[v_fmt or ("q8" if v_q8 else "f16")]
+    vcode = {"f16": 0, "bf16": 1, "q8": 2, "q8t": 3}[v_fmt or ("q8" if v_q8 else "f16")]
     v_q8 = vcode == 2
     q = np.ascontiguousarray(q)
     D = q.shape[-1]

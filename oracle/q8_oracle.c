@@ -228,6 +228,19 @@ void q8o_dequant_row(const uint8_t* row, int D, float* out) {
     }
 }
 
+/* Token `t` of a page-transposed Q8_0 V record (this build's own V layout,
+ * no reference counterpart): fp16 scale of block j at 2*(j*bs + t), int8 of
+ * dim d at 2*(D/32)*bs + d*bs + t.  Same values as q8o_dequant_row of the
+ * token's Q8_0 row. */
+void q8o_dequant_q8t(const uint8_t* rec, int D, int bs, int t, float* out) {
+    const uint8_t* qv = rec + 2 * (D / 32) * bs + t;
+    for (int b = 0; b < D / 32; ++b) {
+        const uint8_t* s = rec + 2 * (b * bs + t);
+        float d = q8o_f16_to_f32((uint16_t)(s[0] | (s[1] << 8)));
+        for (int i = 0; i < 32; ++i) out[b * 32 + i] = (float)(int8_t)qv[(b * 32 + i) * bs] * d;
+    }
+}
+
 /* ----------------------------------------------------------------------- */
 /* Attention reference                                                     */
 /* ----------------------------------------------------------------------- */
@@ -315,7 +328,9 @@ void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_t
                 l += p;
                 const int phys = block_table[(int64_t)b * max_blocks + k / bs];
                 const uint8_t* vr = v_cache + phys * v_page_stride + (k % bs) * v_tok_stride + h * v_head_stride;
-                if (v_fmt == 2) {
+                if (v_fmt == 3) {
+                    q8o_dequant_q8t(v_cache + phys * v_page_stride + h * v_head_stride, D, bs, k % bs, vrow);
+                } else if (v_fmt == 2) {
                     q8o_dequant_row(vr, D, vrow);
                 } else {
                     const uint16_t* v16 = (const uint16_t*)vr;

@@ -10,7 +10,8 @@ ATOL, RTOL = 2e-3, 1e-2          # |out - ref| <= ATOL + RTOL * |ref| (fp32 dequ
 
 class PagedCase:
     """Random paged Q8_0 cache for B sequences: K quantised by the device
-    store kernel (bit-exact with the oracle), V fp16 / bf16 / Q8_0."""
+    store kernel (bit-exact with the oracle), V fp16 / bf16 / Q8_0 token rows
+    ("q8") / Q8_0 page-transposed records ("q8t", [NB, Hkv, bs*D/32*34])."""
 
     def __init__(self, seq_lens, Hkv, D=128, bs=16, v_fmt="f16", seed=0, extra_pages=7,
                  device="cuda", kv_scale=1.0):
@@ -48,6 +49,9 @@ class PagedCase:
         if v_fmt == "q8":
             self.v_cache = torch.zeros((NB, bs, Hkv, rb), dtype=torch.uint8, device=device)
             mode = 2
+        elif v_fmt == "q8t":
+            self.v_cache = torch.zeros((NB, Hkv, bs * rb), dtype=torch.uint8, device=device)
+            mode = 3
         else:
             self.v_cache = torch.zeros((NB, bs, Hkv, D), dtype=vdt, device=device)
             mode = 1
@@ -62,6 +66,8 @@ class PagedCase:
         return 1.0 / float(np.sqrt(self.D))
 
     def _v_strides(self):
+        if self.v_fmt == "q8t":
+            return (self.Hkv * self.bs * self.rb, 0, self.bs * self.rb)
         vb = self.rb if self.v_fmt == "q8" else 2 * self.D
         return (self.bs * self.Hkv * vb, self.Hkv * vb, vb)
 

@@ -48,7 +48,7 @@ def test_direct_decode_gqa(Hq, Hkv):
     assert_close(to_np(out), case.oracle_bhsd(to_np(q), None), what=f"decode {Hq}/{Hkv}")
 
 
-@pytest.mark.parametrize("v_fmt", ["f16", "bf16", "q8"])
+@pytest.mark.parametrize("v_fmt", ["f16", "bf16", "q8", "q8t"])
 @pytest.mark.parametrize("qdt", [torch.float32, torch.float16, torch.bfloat16])
 def test_direct_decode_formats(v_fmt, qdt):
     lens = [5000, 77, 1, 2049]
@@ -57,6 +57,22 @@ def test_direct_decode_formats(v_fmt, qdt):
     out = _direct(case, q)
     qn, tag = _qnp(q)
     assert_close(to_np(out), case.oracle_bhsd(qn, tag), what=f"{v_fmt}/{qdt}")
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(48, 8), (8, 4), (6, 1), (16, 16), (32, 32)])
+@pytest.mark.parametrize("Sq", [1, 4])
+def test_direct_decode_q8t(Hq, Hkv, Sq):
+    """Page-transposed Q8_0 V across kv-head group sizes (1, 4, 8 heads per
+    CTA and several CTAs per sequence), one and two m-tiles."""
+    lens = [4100, 1, 77, 2500, 16, 900]
+    case = PagedCase(lens, Hkv, v_fmt="q8t", seed=Hq + Hkv + Sq)
+    q = _q((len(lens), Hq, Sq, 128), torch.bfloat16, seed=Sq)
+    qa = (case.seq_lens - Sq).astype(np.int32)
+    kw = {"q_abs_offset": torch.from_numpy(qa).to(dev)} if Sq > 1 else {}
+    out = _direct(case, q, **kw)
+    qn, tag = _qnp(q)
+    assert_close(to_np(out), case.oracle_bhsd(qn, tag, q_abs=qa if Sq > 1 else None),
+                 what=f"q8t {Hq}/{Hkv} Sq={Sq}")
 
 
 @pytest.mark.parametrize("Sq", [2, 4, 5])

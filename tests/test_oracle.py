@@ -160,3 +160,45 @@ def test_attention_bhsd_matches_direct_numpy(v_kind):
     for b in range(B):
         ref = _np_attention(q[b], kd[b], v_deq[b], 0.125, int(kv_max[b]), int(qa[b]))
         assert np.abs(o[b] - ref).max() < 1e-5
+
+
+def test_q8t_layout_matches_q8_rows():
+    """The page-transposed Q8_0 V records (store_v_q8t) hold exactly the
+    blocks of the Q8_0 row store: attention over either layout is identical,
+    and every record byte maps back to its row byte."""
+    rng = np.random.default_rng(5)
+    Hkv, D, bs, NB = 2, 128, 16, 9
+    lens = np.array([40, 75], np.int32)
+    T = int(lens.sum())
+    val = rng.standard_normal((T, Hkv, D)).astype(np.float16)
+    key = rng.standard_normal((T, Hkv, D)).astype(np.float16)
+    perm = rng.permutation(NB).astype(np.int32)
+    bt = np.full((2, 5), -1, np.int32)
+    bt[0, :3], bt[1, :5] = perm[:3], perm[3:8]
+    slots = np.concatenate([bt[0, np.arange(40) // bs] * bs + np.arange(40) % bs,
+                            bt[1, np.arange(75) // bs] * bs + np.arange(75) % bs]).astype(np.int64)
+    rb = O.row_bytes(D)
+    k_cache = np.zeros((NB, bs, Hkv, rb), np.uint8)
+    O.reshape_and_cache(key, slots, k_cache)
+    v_rows = np.zeros((NB, bs, Hkv, rb), np.uint8)
+    O.reshape_and_cache(val, slots, v_rows)
+    v_rec = np.zeros((NB, Hkv, bs * rb), np.uint8)
+    O.store_v_q8t(val, slots, v_rec, bs)
+    nb = D // 32
+    for page in range(NB):
+        for h in range(Hkv):
+            for t in range(bs):
+                row = v_rows[page, t, h].reshape(nb, 34)
+                rec = v_rec[page, h]
+                for j in range(nb):
+                    assert rec[2 * (j * bs + t)] == row[j, 0] and rec[2 * (j * bs + t) + 1] == row[j, 1]
+                    got = rec[2 * nb * bs + (j * 32) * bs + t:2 * nb * bs + (j * 32 + 32) * bs + t:bs]
+                    assert np.array_equal(got, row[j, 2:])
+    q = rng.standard_normal((T, 8, D)).astype(np.float16)
+    q_start = np.array([0, 40], np.int32)
+    args = (q, None, q_start, lens, k_cache)
+    kw = dict(q_abs=np.zeros(2, np.int32))
+    a = O.attention_paged(*args, v_rows, bt, lens, 0.088, Hkv, v_fmt="q8", **kw)
+    b = O.attention_paged(*args, v_rec, bt, lens, 0.088, Hkv, v_fmt="q8t",
+                          v_strides=(Hkv * bs * rb, 0, bs * rb), **kw)
+    assert np.array_equal(a, b)

@@ -60,7 +60,7 @@ def test_varlen_without_host_lengths():
                  what="mixed")
 
 
-@pytest.mark.parametrize("v_fmt", ["q8", "bf16"])
+@pytest.mark.parametrize("v_fmt", ["q8", "q8t", "bf16"])
 def test_prefill_v_formats(v_fmt):
     lens, nq = [640], [640]
     case = PagedCase(lens, 8, v_fmt=v_fmt, seed=2)

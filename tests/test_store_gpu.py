@@ -136,6 +136,29 @@ def test_store_kv_fused(vdtype, v_mode):
         assert np.array_equal(got[:, 1].view(np.uint16), ref_v)
 
 
+@pytest.mark.parametrize("vdtype", [torch.float16, torch.bfloat16])
+def test_store_kv_q8_page_transposed(vdtype):
+    """V quantised into page-transposed Q8_0 records [NB, Hkv, bs*D/32*34]:
+    the same blocks as the Q8_0 row store, placed per (page, head) as
+    scales [D/32][bs] then int8 [D][bs]; K unchanged; slot -1 skipped."""
+    T, Hkv, D, NB, bs = 50, 8, 128, 12, 16
+    key = _rand((T, Hkv, D), vdtype, seed=12)
+    val = _rand((T, Hkv, D), vdtype, seed=13, outliers=0.01)
+    slots = torch.randperm(NB * bs, generator=torch.Generator().manual_seed(3))[:T].to(torch.int64)
+    slots[7] = -1
+    rb = D // 32 * 34
+    k_cache = torch.zeros((NB, bs, Hkv, rb), dtype=torch.uint8, device=dev)
+    v_cache = torch.zeros((NB, Hkv, bs * rb), dtype=torch.uint8, device=dev)
+    _gfx().store_kv(key.to(dev), val.to(dev), slots.to(dev), k_cache, v_cache, 3)
+    tag = "bf16" if vdtype == torch.bfloat16 else None
+    ref_k = np.zeros((NB, bs, Hkv, rb), np.uint8)
+    O.reshape_and_cache(to_np(key), slots.numpy(), ref_k, tag)
+    assert np.array_equal(to_np(k_cache), ref_k)
+    ref_v = np.zeros((NB, Hkv, bs * rb), np.uint8)
+    O.store_v_q8t(to_np(val), slots.numpy(), ref_v, bs, tag)
+    assert np.array_equal(to_np(v_cache), ref_v)
+
+
 def test_store_kv_through_c_abi():
     """Same store, called directly through the C ABI with raw pointers."""
     import ctypes
