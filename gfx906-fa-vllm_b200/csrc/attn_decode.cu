@@ -59,7 +59,8 @@ struct DecodeParams {
   int G;                  // query heads per kv head
   int HG;                 // kv heads per CTA
   int HGN;                // head groups (num_heads_kv / HG)
-  int P;                  // pages per stage (= warps per head)
+  int P;                  // pages per stage (= PPW * warps per head)
+  int ppw;                // pages per compute warp per stage
   int CP;                 // pages per chunk (multiple of P)
   int S_max;              // chunks per sequence (upper bound)
   int n_items;
@@ -115,8 +116,8 @@ __device__ __forceinline__ void named_sync_compute() {
 
 // MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0 rows,
 // 3 Q8_0 page-transposed records).
-// NST: shared-memory pipeline slots.
-template <int MT, int VT, bool MASK, int NST>
+// NST: shared-memory pipeline slots.  PPW: pages per compute warp per stage.
+template <int MT, int VT, bool MASK, int NST, int PPW>
 __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodeParams d) {
   using namespace dec;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -457,7 +458,6 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     const int page0 = meta[slot].page0;
     const int npages = meta[slot].npages;
     const bool last = meta[slot].last != 0;
-    const bool page_ok = sub < npages && meta[slot].ok[sub];
     if (item != cur_item) {
       cur_item = item;
       decode_item(d, item, cb, cz, cs);
@@ -470,9 +470,22 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
       reset_state();
       load_q(cb, cz * d.HG + hl);
     }
-    if (page_ok) {
-      const int pg = page0 + sub;
-      const int k0 = pg * PAGE;
+    // This warp's page slots sub*PPW .. +PPW-1 of the stage.  The pages are
+    // processed together, branch-free, so their loads, conversions and MMAs
+    // interleave.  A slot without a valid page reads the data of a valid one
+    // (finite values) and has all its scores masked to -inf.
+    bool pok[PPW];
+    int first_ok = -1;
+#pragma unroll
+    for (int pp = PPW - 1; pp >= 0; --pp) {
+      const int s = sub * PPW + pp;
+      pok[pp] = s < npages && meta[slot].ok[s];
+      if (pok[pp]) first_ok = pp;
+    }
+    if (first_ok >= 0) {
+      int psrc[PPW];
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) psrc[pp] = sub * PPW + (pok[pp] ? pp : first_ok);
       // Key order: accumulator column n of n-tile nt (k-slot nt*8 + n of the
       // P.V product) is physical key 4*(n/2) + e, e = {0,3} for nt = 0 and
       // {1,2} for nt = 1 (by n & 1).  An n-tile then takes one key of each
@@ -483,16 +496,20 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
       auto kaddr = [&](int key) { return (uint32_t)((key >> 2) * d.kgs + (key & 3) * hgb_k); };
       auto vaddr = [&](int key) { return (uint32_t)((key >> 1) * d.vgs + (key & 1) * hgb_v); };
       auto slot_key = [](int nt, int n) { return 4 * (n >> 1) + (nt == 0 ? 3 * (n & 1) : 1 + (n & 1)); };
-      const uint32_t kb = smem_base + slot * d.stage_bytes + sub * d.kpage + hl * d.rb_k;
-      const uint32_t vb = smem_base + slot * d.stage_bytes + d.P * d.kpage + sub * d.vpage + hl * d.rb_v;
+      const uint32_t stage_base = smem_base + slot * d.stage_bytes;
       // ---------------- S = Q K^T --------------------------------------------
-      float sacc[MT][2][4];
+      float sacc[PPW][MT][2][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+      for (int pp = 0; pp < PPW; ++pp)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) sacc[mt][nt][c] = 0.f;
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) sacc[pp][mt][nt][c] = 0.f;
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) {
+      const uint32_t kb = stage_base + psrc[pp] * d.kpage + hl * d.rb_k;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const uint32_t krow = kb + kaddr(slot_key(nt, rq));              // B operand row (key)
@@ -516,24 +533,23 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             q_frag(mt, 2 * blk + 1, a1);
             mma_f16_16816(acc, a0, b0);
             mma_f16_16816(acc, a1, b1);
-            sacc[mt][nt][0] = fmaf(acc[0], dk0, sacc[mt][nt][0]);
-            sacc[mt][nt][1] = fmaf(acc[1], dk1, sacc[mt][nt][1]);
-            sacc[mt][nt][2] = fmaf(acc[2], dk0, sacc[mt][nt][2]);
-            sacc[mt][nt][3] = fmaf(acc[3], dk1, sacc[mt][nt][3]);
+            sacc[pp][mt][nt][0] = fmaf(acc[0], dk0, sacc[pp][mt][nt][0]);
+            sacc[pp][mt][nt][1] = fmaf(acc[1], dk1, sacc[pp][mt][nt][1]);
+            sacc[pp][mt][nt][2] = fmaf(acc[2], dk0, sacc[pp][mt][nt][2]);
+            sacc[pp][mt][nt][3] = fmaf(acc[3], dk1, sacc[pp][mt][nt][3]);
           }
         }
       }
+      }
       // ---------------- mask + online softmax (base 2) ------------------------
-      // pages every row sees completely need no per-element mask
-      const bool page_full = !MASK && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1);
       // Lazy running max: a row keeps its reference max m until one of its
       // scores exceeds m by more than 2^8; only then (rare after the first
       // pages) is the row max reduced over the quad and O / l rescaled.  So
       // P <= 2^8, and the usual page needs no shuffles and no rescale.
-      uint32_t pa[MT][4];
+      uint32_t pa[PPW][MT][4];
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt) {
-        float tmx[2];
+        float tmx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int r = mt * 16 + rq + hh * 8;
@@ -541,25 +557,29 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           int kv_lim = ckv;                                      // exclusive
           if (p.q_abs) kv_lim = min(kv_lim, cqabs + t + 1);
           if (r >= cR) kv_lim = -1;
-          float mx = -INFINITY;
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
+          for (int pp = 0; pp < PPW; ++pp) {
+            const int k0 = (page0 + sub * PPW + pp) * PAGE;
+            // pages every row sees completely need no per-element mask
+            const bool page_full = !MASK && pok[pp] && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              float x = sacc[mt][nt][hh * 2 + c] * d.scale_log2;
-              if (!page_full) {
-                const int k = k0 + 4 * j4 + (nt == 0 ? 3 * c : 1 + c);   // physical key of column 2*j4 + c
-                if constexpr (MASK) {
-                  if (r < cR && k < ckv)
-                    x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
-                        (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int c = 0; c < 2; ++c) {
+                float x = sacc[pp][mt][nt][hh * 2 + c] * d.scale_log2;
+                if (!page_full) {
+                  const int k = k0 + 4 * j4 + (nt == 0 ? 3 * c : 1 + c);   // physical key of column 2*j4 + c
+                  if constexpr (MASK) {
+                    if (pok[pp] && r < cR && k < ckv)
+                      x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                          (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+                  }
+                  x = (pok[pp] && k < kv_lim) ? x : -INFINITY;
                 }
-                x = k < kv_lim ? x : -INFINITY;
+                sacc[pp][mt][nt][hh * 2 + c] = x;
+                tmx[hh] = fmaxf(tmx[hh], x);
               }
-              sacc[mt][nt][hh * 2 + c] = x;
-              mx = fmaxf(mx, x);
-            }
-          tmx[hh] = mx;
+          }
         }
         const bool grow = tmx[0] > mrow[mt][0] + kRescaleLog2 || tmx[1] > mrow[mt][1] + kRescaleLog2;
         if (__any_sync(0xffffffffu, grow)) {
@@ -589,28 +609,36 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           const float mu = mrow[mt][hh] == -INFINITY ? 0.f : mrow[mt][hh];
           float ls = 0.f;
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
+          for (int pp = 0; pp < PPW; ++pp)
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const float pv = fast_exp2(sacc[mt][nt][hh * 2 + c] - mu);
-              sacc[mt][nt][hh * 2 + c] = pv;
-              ls += pv;
-            }
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int c = 0; c < 2; ++c) {
+                const float pv = fast_exp2(sacc[pp][mt][nt][hh * 2 + c] - mu);
+                sacc[pp][mt][nt][hh * 2 + c] = pv;
+                ls += pv;
+              }
           lrow[mt][hh] += ls;
         }
-        if constexpr (VT == 1) {
-          pa[mt][0] = pack_bf162(sacc[mt][0][0], sacc[mt][0][1]);
-          pa[mt][1] = pack_bf162(sacc[mt][0][2], sacc[mt][0][3]);
-          pa[mt][2] = pack_bf162(sacc[mt][1][0], sacc[mt][1][1]);
-          pa[mt][3] = pack_bf162(sacc[mt][1][2], sacc[mt][1][3]);
-        } else {
-          pa[mt][0] = pack_half2(sacc[mt][0][0], sacc[mt][0][1]);
-          pa[mt][1] = pack_half2(sacc[mt][0][2], sacc[mt][0][3]);
-          pa[mt][2] = pack_half2(sacc[mt][1][0], sacc[mt][1][1]);
-          pa[mt][3] = pack_half2(sacc[mt][1][2], sacc[mt][1][3]);
+#pragma unroll
+        for (int pp = 0; pp < PPW; ++pp) {
+          if constexpr (VT == 1) {
+            pa[pp][mt][0] = pack_bf162(sacc[pp][mt][0][0], sacc[pp][mt][0][1]);
+            pa[pp][mt][1] = pack_bf162(sacc[pp][mt][0][2], sacc[pp][mt][0][3]);
+            pa[pp][mt][2] = pack_bf162(sacc[pp][mt][1][0], sacc[pp][mt][1][1]);
+            pa[pp][mt][3] = pack_bf162(sacc[pp][mt][1][2], sacc[pp][mt][1][3]);
+          } else {
+            pa[pp][mt][0] = pack_half2(sacc[pp][mt][0][0], sacc[pp][mt][0][1]);
+            pa[pp][mt][1] = pack_half2(sacc[pp][mt][0][2], sacc[pp][mt][0][3]);
+            pa[pp][mt][2] = pack_half2(sacc[pp][mt][1][0], sacc[pp][mt][1][1]);
+            pa[pp][mt][3] = pack_half2(sacc[pp][mt][1][2], sacc[pp][mt][1][3]);
+          }
         }
       }
       // ---------------- O += P V ------------------------------------------------
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) {
+      const uint32_t vb = stage_base + d.P * d.kpage + psrc[pp] * d.vpage + hl * d.rb_v;
       if constexpr (VT < 2) {
         // ldmatrix.trans: thread i addresses matrix i/8 row i%8; matrices
         // (keys 0-7 | 8-15) x (d block nt | nt+1)
@@ -625,11 +653,11 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             if constexpr (VT == 1) {
-              mma_bf16_16816(o[mt][2 * ntp], pa[mt], bA);
-              mma_bf16_16816(o[mt][2 * ntp + 1], pa[mt], bB);
+              mma_bf16_16816(o[mt][2 * ntp], pa[pp][mt], bA);
+              mma_bf16_16816(o[mt][2 * ntp + 1], pa[pp][mt], bB);
             } else {
-              mma_f16_16816(o[mt][2 * ntp], pa[mt], bA);
-              mma_f16_16816(o[mt][2 * ntp + 1], pa[mt], bB);
+              mma_f16_16816(o[mt][2 * ntp], pa[pp][mt], bA);
+              mma_f16_16816(o[mt][2 * ntp + 1], pa[pp][mt], bB);
             }
           }
         }
@@ -640,7 +668,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         // (2*j4+8, 2*j4+9) = keys (4*j4+1, 4*j4+2) (the key order above), so
         // a byte permute builds each pair.  int8 -> fp16 is exact
         // ((0x6400 | (b ^ 0x80)) - 1152); the scale is applied in fp16.
-        const uint32_t vrec = smem_base + slot * d.stage_bytes + d.P * d.kpage + sub * d.vpage + hl * d.vrec;
+        const uint32_t vrec = stage_base + d.P * d.kpage + psrc[pp] * d.vpage + hl * d.vrec;
         const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
@@ -660,7 +688,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             const __half2 x1 = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&t1), bias), s12);
             const uint32_t bq[2] = {*reinterpret_cast<const uint32_t*>(&x0), *reinterpret_cast<const uint32_t*>(&x1)};
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][blk * 4 + m], pa[mt], bq);
+            for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][blk * 4 + m], pa[pp][mt], bq);
           }
         }
       } else {
@@ -686,9 +714,10 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             __half2 x89 = __hmul2(*reinterpret_cast<__half2*>(&h89), s89);
             const uint32_t bq[2] = {*reinterpret_cast<uint32_t*>(&x01), *reinterpret_cast<uint32_t*>(&x89)};
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][nt], pa[mt], bq);
+            for (int mt = 0; mt < MT; ++mt) mma_f16_16816(o[mt][nt], pa[pp][mt], bq);
           }
         }
+      }
       }
     }
     __syncwarp();
@@ -770,6 +799,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   d.HG = Hkv % 8 == 0 ? 8 : (Hkv % 4 == 0 ? 4 : (Hkv % 2 == 0 ? 2 : 1));
   if (Hkv > 8 && d.HG != 8) return cudaErrorInvalidValue;
   d.HGN = Hkv / d.HG;
+  d.ppw = 1;
   d.P = NWC / d.HG;
   d.rb_k = q8_row_bytes(D);
   const bool vq8t = p.v_fmt == G9_VFMT_Q8T;
@@ -803,13 +833,26 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // page-transposed V: the HG records back to back (ldmatrix rows are 16
   // consecutive bytes, conflict-free at any 16-byte aligned base)
   d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
-  d.stage_bytes = d.P * (d.kpage + d.vpage);
   const int wph = NWC / d.HG;
   const int merge_bytes = wph > 1 ? d.HG * mt * (16 * 4 + 4) * 32 * 4 : 0;
   const int q_bytes = mt == 2 ? d.HG * mt * 16 * QROW : 0;
-  // 4 slots when they fit in shared memory (227 KB per CTA), else 3
-  d.nst = MAXST;
-  if ((int64_t)d.nst * d.stage_bytes + merge_bytes + q_bytes > 227 * 1024) d.nst = 3;
+  constexpr int64_t kSmem = 227 * 1024;
+  auto need = [&](int nst, int pages) {
+    return (int64_t)nst * pages * (d.kpage + d.vpage) + merge_bytes + q_bytes;
+  };
+  // Two pages per warp and stage give each warp two independent streams of
+  // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
+  // (one m-tile only: with two the registers would spill); else one page per
+  // warp with 4 stages, or 3 when 4 do not fit.
+  if (mt == 1 && 2 * d.P <= MAXP && need(3, 2 * d.P) <= kSmem) {
+    d.ppw = 2;
+    d.P *= 2;
+    d.nst = 3;
+  } else {
+    d.nst = need(MAXST, d.P) <= kSmem ? MAXST : 3;
+    if (need(d.nst, d.P) > kSmem) return cudaErrorInvalidValue;
+  }
+  d.stage_bytes = d.P * (d.kpage + d.vpage);
   d.merge_off = d.nst * d.stage_bytes;
   d.q_off = d.merge_off + merge_bytes;
   d.scale_log2 = p.scale * kLog2e;
@@ -835,7 +878,10 @@ static size_t decode_ws_bytes(const DecodeParams& d) {
 template <int MT, int VT, bool MASK>
 static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)d.HG * MT * 16 * dec::QROW : 0);
-  auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4> : decode_kernel<MT, VT, MASK, 3>;
+  auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4, 1> : decode_kernel<MT, VT, MASK, 3, 1>;
+  if constexpr (MT == 1) {
+    if (d.ppw == 2) kern = decode_kernel<MT, VT, MASK, 3, 2>;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::max(1, std::min(d.n_items, num_sms()));
