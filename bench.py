@@ -143,12 +143,12 @@ def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
     return k_cache, v_cache, bt
 
 
-# DRAM bytes (read + write) of one decode_kernel launch per algorithmic byte:
-# ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum on the first 16
-# sequences of config 3 (fp16 V) read 666.97 MB and wrote 20.39 MB against
-# 666.14 MB of algorithmic bytes (K rows, V rows, Q, O, block table).  The
-# excess is the split-K partials.
-DECODE_TRAFFIC_RATIO = (666.97 + 20.39) / 666.14
+# DRAM bytes (read + write) of one decode_kernel launch per algorithmic byte,
+# from ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum on the first
+# 16 sequences of config 3: page-transposed Q8_0 V read 462.75 MB and wrote
+# 21.81 MB against 462.36 MB of algorithmic bytes; fp16 V read 666.97 MB and
+# wrote 20.39 MB against 666.14 MB.  The writes are the split-K partials.
+DECODE_TRAFFIC_RATIO = {"q8_0": (462.75 + 21.81) / 462.36, "fp16": (666.97 + 20.39) / 666.14}
 
 
 def decode_bytes(lens, hkv, hq, v_row=256):
@@ -170,10 +170,11 @@ def prefill_flops(n_tokens, chunk, hq):
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle restatement, test infrastructure)
 # ---------------------------------------------------------------------------
-def cpu_baseline(seconds_target=10.0, threads=None):
+def cpu_baseline(seconds_target=10.0, threads=None, v_fmt="q8_0"):
     """Oracle attention (fp32 dequant + softmax, double accumulation) on the
     host cores over a bounded sample of config 3: the first sequences until
-    ~seconds_target of work.  Returns GB/s in the decode metric's bytes."""
+    ~seconds_target of work.  Returns GB/s in the decode metric's bytes.
+    v_fmt "q8_0": page-transposed Q8_0 V records; else fp16 V rows."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     threads = threads or os.cpu_count()
@@ -186,14 +187,22 @@ def cpu_baseline(seconds_target=10.0, threads=None):
         kq = rng.integers(0, 256, size=(nb, BS, HKV, RB), dtype=np.uint8)
         kq[..., 0::34] = 0x00          # small scales keep the values finite
         kq[..., 1::34] = 0x20
-        vc = rng.standard_normal((nb, BS, HKV, D)).astype(np.float16)
         q = rng.standard_normal((1, HQ, D)).astype(np.float32)
         bt = np.arange(nb, dtype=np.int32).reshape(1, nb)
+        if v_fmt == "q8_0":
+            vc = rng.integers(0, 256, size=(nb, HKV, BS * RB), dtype=np.uint8)
+            vc[..., :2 * (D // 32) * BS:2] = 0x00    # fp16 scales 0x2000: small, finite
+            vc[..., 1:2 * (D // 32) * BS:2] = 0x20
+            kw = dict(v_fmt="q8t", v_strides=(HKV * BS * RB, 0, BS * RB))
+            v_row = RB
+        else:
+            vc = rng.standard_normal((nb, BS, HKV, D)).astype(np.float16)
+            kw, v_row = {}, 2 * D
         t0 = time.perf_counter()
         O.attention_paged(q, None, np.array([0]), np.array([1]), kq, vc, bt, np.array([L]), 1 / np.sqrt(D),
-                          HKV, nthreads=threads)
+                          HKV, nthreads=threads, **kw)
         elapsed += time.perf_counter() - t0
-        done_bytes += decode_bytes([L], HKV, HQ)
+        done_bytes += decode_bytes([L], HKV, HQ, v_row)
         nseq += 1
         if elapsed > seconds_target:
             break
@@ -210,7 +219,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-prefill", action="store_true")
-    ap.add_argument("--v-fmt", default="fp16", choices=["fp16", "q8_0", "q8_0rows"])
+    ap.add_argument("--v-fmt", default="q8_0", choices=["fp16", "q8_0", "q8_0rows"],
+                    help="V cache format: q8_0 = page-transposed Q8_0 (config 3's Q8_0 K/V cache)")
+    ap.add_argument("--no-fp16v", action="store_true", help="skip the extra fp16-V decode measurement")
     ap.add_argument("--decode-seqs", type=int, default=64,
                     help="first N sequences of config 3 (profiling uses a smaller case)")
     ap.add_argument("--prefill-tokens", type=int, default=32768)
@@ -224,12 +235,13 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        res, el = cpu_baseline(seconds_target=max(3.0, min(20.0, 2.0 * args.steps)))
+        res, el = cpu_baseline(seconds_target=max(3.0, min(20.0, 2.0 * args.steps)), v_fmt=args.v_fmt)
         line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
                 "impl": "reference",
-                "config": {"workload": "config3 decode (64 seqs, L~U[1K,32K], GQA 48/8, d128, Q8_0 K)",
+                "config": {"workload": "config3 decode (64 seqs, L~U[1K,32K], GQA 48/8, d128, Q8_0 K, "
+                                       + ("Q8_0 V" if args.v_fmt.startswith("q8_0") else "fp16 V") + ")",
                            "sample": res["sample"]},
                 "cpu_baseline": res,
                 "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -340,13 +352,41 @@ def main():
     d2h = out_host.numel() * 2
     e2e_value = bytes_all / (e2e_ms * 1e-3) / 1e9
 
+    # ---------------- same decode with fp16 V (reference parity mode) -------
+    fp16v = None
+    if args.v_fmt != "fp16" and not args.no_fp16v:
+        v_cache = None
+        torch.cuda.empty_cache()
+        k2, v2, bt2 = build_cache(lens, hkv, seed=3000 + rank, device=device, v_fmt="fp16")
+
+        def decode_fp16v():
+            gfx906_fa.paged_attention(q, k2, v2, bt2, sl, cu, 1, max_l, scale, out=out,
+                                      query_lens_host=ones, seq_lens_host=lens_l)
+
+        for _ in range(max(3, args.warmup)):
+            decode_fp16v()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(args.steps):
+            decode_fp16v()
+        f1.record()
+        barrier()
+        fms = max_over_ranks(f0.elapsed_time(f1)) / args.steps
+        fb = decode_bytes(lens, hkv, hq, 2 * D)
+        fp16v = {"value": fb * world / (fms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": fms,
+                 "frac_of_hbm": fb / (fms * 1e-3) / 1e9 / hbm_peak,
+                 "workload": "config3 decode with fp16 V rows (the reference's V format)"}
+        del k2, v2, bt2
+        torch.cuda.empty_cache()
+
     # ---------------- prefill (config 4 at 32K) -----------------------------
     prefill = None
     if not args.no_prefill:
         N, C = args.prefill_tokens, 8192
         del k_cache, v_cache
         torch.cuda.empty_cache()
-        kc, vc, btp = build_cache([N], hkv, seed=2000 + rank, device=device)
+        kc, vc, btp = build_cache([N], hkv, seed=2000 + rank, device=device, v_fmt=args.v_fmt)
         qp = torch.randn((N, hq, D), generator=gq, device=device).to(torch.bfloat16)
         op = torch.empty_like(qp)
         chunks = []
@@ -374,7 +414,8 @@ def main():
         fl_all = prefill_flops(N, C, HQ)
         tfs = fl_all / (pms * 1e-3) / 1e12
         prefill = {"value": tfs, "unit": "TFLOP/s", "ms_per_step": pms,
-                   "workload": f"config4: 1 seq x {N} tokens, 8192-query chunks, causal, GQA 48/8",
+                   "workload": f"config4: 1 seq x {N} tokens, 8192-query chunks, causal, GQA 48/8, "
+                               f"{'Q8_0' if args.v_fmt.startswith('q8_0') else 'fp16'} V",
                    "roofline": {"bound": "tensor", "achieved": fl_all / world / (pms * 1e-3) / 1e12,
                                 "peak": tf_peak, "unit": "TFLOP/s",
                                 "frac": fl_all / world / (pms * 1e-3) / 1e12 / tf_peak,
@@ -383,7 +424,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu, _ = cpu_baseline(seconds_target=10.0)
+        cpu, _ = cpu_baseline(seconds_target=10.0, v_fmt=args.v_fmt)
 
     if rank == 0:
         line = {
@@ -399,7 +440,8 @@ def main():
                        "l2": "inputs (%.2f GB per GPU) larger than L2, no flush" % (bytes_rank / 1e9)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak,
-                         "traffic": bytes_rank * DECODE_TRAFFIC_RATIO,
+                         "traffic": (bytes_rank * DECODE_TRAFFIC_RATIO[args.v_fmt]
+                                     if args.v_fmt in DECODE_TRAFFIC_RATIO else None),
                          "traffic_note": "ncu dram read+write of decode_kernel on the 16-sequence prefix of "
                                          "this workload, scaled by the algorithmic bytes",
                          "peak_kind": f"{peak_kind} copy bandwidth"},
@@ -408,6 +450,8 @@ def main():
             "gpu_launches": 2 * args.steps,
             "clocks": sampler.summary(),
         }
+        if fp16v:
+            line["decode_fp16_v"] = fp16v
         if prefill:
             line["prefill"] = prefill
         if cpu:

@@ -68,7 +68,9 @@ def kv_cache_views(kv_cache: torch.Tensor, v_fmt: str = "fp16"):
     k_q8: uint8 [NB, bs, Hkv, D/32*34] -- dense Q8_0 rows at the start of
           each page's K half;
     v:    the V half [NB, bs, Hkv, D] (fp16 mode) or uint8
-          [NB, bs, Hkv, D/32*34] at the start of each page's V half (q8_0).
+          [NB, Hkv, bs*D/32*34] page-transposed Q8_0 records at the start of
+          each page's V half (q8_0): per kv head the fp16 block scales
+          [D/32][bs], then the int8 values [D][bs].
     """
     NB, two, bs, Hkv, D = kv_cache.shape
     rb = q8_row_bytes(D)
@@ -76,7 +78,7 @@ def kv_cache_views(kv_cache: torch.Tensor, v_fmt: str = "fp16"):
     raw = kv_cache.view(torch.uint8).view(NB, 2, page)
     k_q8 = raw[:, 0, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
     if v_fmt == "q8_0":
-        v = raw[:, 1, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
+        v = raw[:, 1, :bs * Hkv * rb].view(NB, Hkv, bs * rb)
     else:
         v = kv_cache[:, 1]
     return k_q8, v
@@ -264,7 +266,7 @@ class Gfx906FAImpl(AttentionImpl):
             return
         n = slots.shape[0]
         k_q8, v = kv_cache_views(kv_cache, self._v_fmt)
-        gfx906_fa.store_kv(key[:n], value[:n], slots, k_q8, v, 2 if self._v_fmt == "q8_0" else 1)
+        gfx906_fa.store_kv(key[:n], value[:n], slots, k_q8, v, 3 if self._v_fmt == "q8_0" else 1)
 
     # ------------------------------------------------------------------
     # Forward

@@ -88,7 +88,8 @@ def _gather_kv_q8(key_cache_q8: torch.Tensor, value_cache: torch.Tensor, block_t
 def forward_paged(
     query: torch.Tensor,            # [num_tokens, Hq, D]
     key_cache: torch.Tensor,        # [num_blocks, block_size, Hkv, D]  16-bit (legacy path only)
-    value_cache: torch.Tensor,      # [num_blocks, block_size, Hkv, D]  16-bit (or Q8_0 bytes)
+    value_cache: torch.Tensor,      # [num_blocks, block_size, Hkv, D]  16-bit (or Q8_0 bytes), or
+                                    # [num_blocks, Hkv, block_size*(D/32)*34] page-transposed Q8_0
     block_table: torch.Tensor,      # [num_seqs, max_blocks]            int32
     seq_lens: torch.Tensor,         # [num_seqs]                        int32
     cu_seqlens_q: torch.Tensor,     # [num_seqs+1]                      int32
@@ -122,7 +123,9 @@ def forward_paged(
     cu = cu_seqlens_q if cu_seqlens_q.dtype == torch.int32 else cu_seqlens_q.to(torch.int32)
     cu = cu.contiguous()
 
-    if key_cache_q8 is not None and _should_use_direct_paged(num_seqs, max_seqlen_q):
+    # page-transposed Q8_0 V is only read by the direct kernels
+    v_q8t = value_cache is not None and value_cache.dim() == 3
+    if key_cache_q8 is not None and (v_q8t or _should_use_direct_paged(num_seqs, max_seqlen_q)):
         if _DBG:
             _fwdlog(f"forward_paged DIRECT: T={num_tokens} Hq={Hq} B={num_seqs} "
                     f"max_q={max_seqlen_q} max_k={max_seqlen_k}")
