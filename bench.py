@@ -259,9 +259,9 @@ def main():
         dist.init_process_group("nccl")
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    assert HKV % world == 0, "kv heads must split evenly"
-    hkv = HKV // world
-    hq = HQ // world
+    from gfx906_fa_shard import head_shard
+    shard = head_shard(HQ, HKV, world, rank)      # vLLM-style tensor-parallel head groups
+    hkv, hq = shard.num_heads_kv, shard.num_heads_q
 
     # ---------------- decode workload (config 3) ----------------------------
     lens = config3_lens()[:args.decode_seqs]

@@ -24,10 +24,11 @@
 //    roundings beyond fp32 are Q and P to 16 bits and, for Q8_0 V, the
 //    dequantised V to fp16.
 //  * With fewer than 8 kv heads per CTA, the warps of one head split the
-//    pages of a stage and merge their softmax states at the end of a chunk.
-//  * A chunk's result is final when the sequence has one chunk; otherwise
-//    the normalised partial O and its (max, sum) go to the workspace and a
-//    combine kernel merges them (log-sum-exp weights).
+//    pages of a stage; each keeps its own softmax state.
+//  * A chunk's result is final when the sequence has one chunk and its head
+//    one warp; otherwise each warp's normalised partial O and its (max, sum)
+//    go to the workspace and a combine kernel merges them (log-sum-exp
+//    weights).
 //
 // Masking follows the reference: keys at k >= kv_len are ignored, with
 // q_abs the causal rule is k <= q_abs[b] + t (fattn-q8.cuh:646-654), and an
@@ -63,6 +64,8 @@ struct DecodeParams {
   int ppw;                // pages per compute warp per stage
   int CP;                 // pages per chunk (multiple of P)
   int S_max;              // chunks per sequence (upper bound)
+  int wph;                // compute warps per kv head (they split a chunk's pages)
+  int S_part;             // partial results per (sequence, kv head): S_max * wph
   int n_items;
   int R_pad;              // 16 * MT
   int rb_k, rb_v;         // bytes of one K / V row
@@ -72,14 +75,13 @@ struct DecodeParams {
   int contig;             // 1: rows of consecutive tokens are adjacent (one copy per group)
   int kpage, vpage;       // smem bytes per page
   int stage_bytes;
-  int merge_off;          // smem offset of the merge buffer
   int q_off;              // smem offset of the Q tiles (MT == 2)
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
   int nst;                // pipeline slots of this launch
   float scale_log2;
   unsigned int* counter;  // work-queue counter (zeroed before the launch)
-  float* opart;           // [B][Hkv][S_max][R_pad][D]
-  float2* ml;             // [B][Hkv][S_max][R_pad]
+  float* opart;           // [B][Hkv][S_part][R_pad][D]
+  float2* ml;             // [B][Hkv][S_part][R_pad]
 };
 
 struct StageMeta {
@@ -363,7 +365,6 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     }
   };
 
-  float* merge = reinterpret_cast<float*>(smem + d.merge_off);
 
   auto epilogue = [&]() {
     // quad-reduce the running sums
@@ -376,50 +377,8 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         lrow[mt][hh] = v;
       }
-    // merge the warps that share a kv head (fragment order: lane-contiguous)
-    const int wph = NWC / d.HG;
-    float* mb = merge + (size_t)hl * (MT * (16 * 4 + 4) * 32);
-    for (int rr = 1; rr < wph; ++rr) {
-      if (sub == rr) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-          for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) mb[((mt * 16 + nt) * 4 + c) * 32 + lane] = o[mt][nt][c];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            mb[(MT * 64 + mt * 4 + hh) * 32 + lane] = mrow[mt][hh];
-            mb[(MT * 64 + mt * 4 + 2 + hh) * 32 + lane] = lrow[mt][hh];
-          }
-        }
-      }
-      named_sync_compute();
-      if (sub == 0) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          float a0[2], a1[2];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const float m1 = mb[(MT * 64 + mt * 4 + hh) * 32 + lane];
-            const float l1 = mb[(MT * 64 + mt * 4 + 2 + hh) * 32 + lane];
-            const float mn = fmaxf(mrow[mt][hh], m1);
-            const float mu = mn == -INFINITY ? 0.f : mn;
-            a0[hh] = fast_exp2(mrow[mt][hh] - mu);
-            a1[hh] = fast_exp2(m1 - mu);
-            mrow[mt][hh] = mn;
-            lrow[mt][hh] = lrow[mt][hh] * a0[hh] + l1 * a1[hh];
-          }
-#pragma unroll
-          for (int nt = 0; nt < 16; ++nt)
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              o[mt][nt][c] = o[mt][nt][c] * a0[c >> 1] + mb[((mt * 16 + nt) * 4 + c) * 32 + lane] * a1[c >> 1];
-        }
-      }
-      named_sync_compute();
-    }
-    if (sub != 0) return;
+    // every warp of a head writes its own partial result (the warps split the
+    // chunk's pages); decode_combine_kernel merges them with the other chunks'
     const int h = cz * d.HG + hl;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
@@ -429,7 +388,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         if (r >= cR) continue;
         const float l = lrow[mt][hh];
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        if (cnsplit == 1) {
+        if (cnsplit == 1 && d.wph == 1) {
           const int t = r / d.G;
           const int hq = h * d.G + (r - t * d.G);
           const int64_t ob = o_offset(p, cb, t, hq);
@@ -438,7 +397,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             store_out2(p.out, p.out_dtype, ob + nt * 8 + 2 * j4, o[mt][nt][hh * 2] * inv,
                        o[mt][nt][hh * 2 + 1] * inv);
         } else {
-          const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_max + cs) * d.R_pad + r;
+          const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_part + cs * d.wph + sub) * d.R_pad + r;
           float* op = d.opart + row * D;
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt)
@@ -727,9 +686,16 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
 }
 
 // ---------------------------------------------------------------------------
-// combine: merge the per-chunk partial results of sequences with >1 chunk
+// combine: merge the partial results (per chunk and per warp of a head) of
+// sequences with more than one
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams d) {
+// One CTA per (kv head, sequence), one warp per query row (R <= 32 rows).
+// Lanes reduce the partials' maxima; then, 32 partials at a time, lane j
+// computes the weight l_s * 2^(m_s - M) of partial base + j, and every lane
+// accumulates 4 of the 128 output dims of each partial (weights broadcast by
+// shuffle, 16-byte loads).
+constexpr int kCombineMaxParts = 1024;
+__global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams d) {
   const G9AttnBatch& p = d.p;
   const int b = blockIdx.y;
   const int h = blockIdx.x;
@@ -737,30 +703,45 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams 
   if (nq <= 0 || nq * d.G > d.max_rows) return;
   const int kv_end = seq_kv_end(p, b, nq);
   const int npg = (kv_end + dec::PAGE - 1) / dec::PAGE;
-  const int nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;
+  const int nsplit = (npg == 0 ? 1 : (npg + d.CP - 1) / d.CP) * d.wph;   // partials of this sequence
   if (nsplit <= 1) return;
   const int R = nq * d.G;
-  const int dd = threadIdx.x;
-  for (int r = 0; r < R; ++r) {
-    const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_max) * d.R_pad + r;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
-    const float mu = M == -INFINITY ? 0.f : M;
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float2 ml = d.ml[row0 + (int64_t)s * d.R_pad];
-      const float w = ml.y * fast_exp2(ml.x - mu);
-      den += w;
-      num += w * d.opart[(row0 + (int64_t)s * d.R_pad) * dec::D + dd];
+  const int r = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_part) * d.R_pad + r;
+  float M = -INFINITY;
+  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float mu = M == -INFINITY ? 0.f : M;
+  float den = 0.f;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  const float* op = d.opart + row0 * dec::D + 4 * lane;
+  for (int base = 0; base < nsplit; base += 32) {
+    float w = 0.f;
+    if (base + lane < nsplit) {
+      const float2 ml = d.ml[row0 + (int64_t)(base + lane) * d.R_pad];
+      w = ml.y * fast_exp2(ml.x - mu);
     }
-    const float v = den > 0.f ? num / den : 0.f;
-    const int t = r / d.G;
-    const int hq = h * d.G + (r - t * d.G);
-    const int64_t off = o_offset(p, b, t, hq) + dd;
-    if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = v;
-    else if (p.out_dtype == DT_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(v);
-    else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(v);
+    den += w;
+    const int n = min(32, nsplit - base);          // warp-uniform
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      const float4 v = *reinterpret_cast<const float4*>(op + (int64_t)(base + j) * d.R_pad * dec::D);
+      num.x = fmaf(wj, v.x, num.x); num.y = fmaf(wj, v.y, num.y);
+      num.z = fmaf(wj, v.z, num.z); num.w = fmaf(wj, v.w, num.w);
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const int t = r / d.G;
+  const int hq = h * d.G + (r - t * d.G);
+  const int64_t off = o_offset(p, b, t, hq) + 4 * lane;
+  store_out2(p.out, p.out_dtype, off, num.x * inv, num.y * inv);
+  store_out2(p.out, p.out_dtype, off + 2, num.z * inv, num.w * inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -821,7 +802,8 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   d.contig = p.k_tok_stride == hgk && (vq8t || p.v_tok_stride == hgv);
   if (((uintptr_t)p.k_cache | (uintptr_t)p.v_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.v_page_stride) & 15)
     return cudaErrorInvalidValue;
-  if (((int64_t)d.HG * p.k_head_stride) % 16 || (!vq8t && ((int64_t)d.HG * p.v_head_stride) % 16))
+  // head groups after the first start at h0 = z*HG heads into a token's rows
+  if (d.HGN > 1 && (((int64_t)d.HG * p.k_head_stride) % 16 || (!vq8t && ((int64_t)d.HG * p.v_head_stride) % 16)))
     return cudaErrorInvalidValue;
   if (d.contig) {
     if ((2 * hgk) % 16 || (!vq8t && (2 * hgv) % 16)) return cudaErrorInvalidValue;
@@ -835,12 +817,11 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // page-transposed V: the HG records back to back (ldmatrix rows are 16
   // consecutive bytes, conflict-free at any 16-byte aligned base)
   d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
-  const int wph = NWC / d.HG;
-  const int merge_bytes = wph > 1 ? d.HG * mt * (16 * 4 + 4) * 32 * 4 : 0;
+  d.wph = NWC / d.HG;
   const int q_bytes = mt == 2 ? d.HG * mt * 16 * QROW : 0;
   constexpr int64_t kSmem = 227 * 1024;
   auto need = [&](int nst, int pages) {
-    return (int64_t)nst * pages * (d.kpage + d.vpage) + merge_bytes + q_bytes;
+    return (int64_t)nst * pages * (d.kpage + d.vpage) + q_bytes;
   };
   // Two pages per warp and stage give each warp two independent streams of
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
@@ -855,8 +836,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     if (need(d.nst, d.P) > kSmem) return cudaErrorInvalidValue;
   }
   d.stage_bytes = d.P * (d.kpage + d.vpage);
-  d.merge_off = d.nst * d.stage_bytes;
-  d.q_off = d.merge_off + merge_bytes;
+  d.q_off = d.nst * d.stage_bytes;
   d.scale_log2 = p.scale * kLog2e;
   // chunking: enough chunks to keep every SM busy several times over
   const int sms = num_sms();
@@ -864,15 +844,18 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   const int64_t est_pages = (int64_t)p.num_seqs * d.HGN * max_pages / 2 + 1;   // lengths ~ U[0, max]
   const int64_t want = est_pages / ((int64_t)sms * 6);
   int cp = (int)std::min<int64_t>(std::max<int64_t>(want, 16), 512);
+  // at most kCombineMaxParts partials per (sequence, kv head)
+  cp = std::max<int>(cp, (int)(((int64_t)max_pages * d.wph + kCombineMaxParts - 1) / kCombineMaxParts));
   cp = ((cp + d.P - 1) / d.P) * d.P;
   d.CP = cp;
   d.S_max = max_pages == 0 ? 1 : (max_pages + cp - 1) / cp;
+  d.S_part = d.S_max * d.wph;
   d.n_items = p.num_seqs * d.HGN * d.S_max;
   return cudaSuccess;
 }
 
 static size_t decode_ws_bytes(const DecodeParams& d) {
-  const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+  const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_part * d.R_pad;
   const size_t o = rows * dec::D * sizeof(float);
   return 256 + ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
 }
@@ -890,8 +873,8 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   kern<<<grid, dec::NTHREADS, smem, stream>>>(d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (d.S_max > 1) {
-    decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), dec::D, 0, stream>>>(d);
+  if (d.S_part > 1) {
+    decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows, 0, stream>>>(d);
     e = cudaGetLastError();
   }
   return e;
@@ -922,7 +905,7 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
   if (!workspace || workspace_bytes < decode_ws_bytes(d) || ((uintptr_t)workspace & 15)) return cudaErrorInvalidValue;
   {
     // [0, 256): work-queue counter; then partial O and (max, sum) rows
-    const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+    const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_part * d.R_pad;
     uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
     d.counter = reinterpret_cast<unsigned int*>(w);
     d.opart = reinterpret_cast<float*>(w + 256);

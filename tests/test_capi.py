@@ -54,3 +54,37 @@ def test_extension_exposes_reference_ops():
     m = importlib.import_module("gfx906_fa")
     for name in ("quantize_q8_0", "reshape_and_cache_q8", "gather_paged_kv_q8"):
         assert hasattr(m, name)
+
+
+@pytest.mark.parametrize("hkv", [1, 2, 4, 8, 16])
+@pytest.mark.parametrize("v_fmt", [0, 3])
+def test_decode_plans_dense_pages_for_every_head_count(hkv, v_fmt):
+    """Host-side planning only (no launch): a dense paged decode batch must be
+    accepted by the split-K decode kernel for every kv-head count a tensor-
+    parallel rank can hold (a rejection would silently route decode to the
+    128-row tensor-core prefill kernel).  v_fmt 0: fp16 V rows; 3: page-
+    transposed Q8_0 V records."""
+    from test_zz_no_alloc import G9AttnBatch
+    lib = capi()
+    lib.gfx906_fa_decode_workspace_size.restype = ctypes.c_size_t
+    lib.gfx906_fa_decode_workspace_size.argtypes = [ctypes.POINTER(G9AttnBatch)]
+    D, bs, rb, B = 128, 16, 136, 4
+    b = G9AttnBatch()
+    b.q, b.q_dtype = 1 << 20, 1
+    b.q_seq_stride, b.q_tok_stride, b.q_head_stride = 6 * hkv * D, 0, D
+    b.seq_q = 1
+    b.out, b.out_dtype = 2 << 20, 1
+    b.o_seq_stride, b.o_tok_stride, b.o_head_stride = 6 * hkv * D, 0, D
+    b.k_cache = 3 << 20
+    b.k_page_stride, b.k_tok_stride, b.k_head_stride = 2 * bs * hkv * 2 * D, hkv * rb, rb
+    b.v_cache = 4 << 20
+    if v_fmt == 3:
+        b.v_page_stride, b.v_tok_stride, b.v_head_stride = 2 * bs * hkv * 2 * D, 0, bs * rb
+    else:
+        b.v_page_stride, b.v_tok_stride, b.v_head_stride = 2 * bs * hkv * 2 * D, hkv * 2 * D, 2 * D
+    b.v_fmt = v_fmt
+    b.block_table, b.max_blocks, b.block_size = 5 << 20, 2048, bs
+    b.kv_len, b.max_kv = 6 << 20, 32768
+    b.num_seqs, b.num_heads_q, b.num_heads_kv, b.head_dim = B, 6 * hkv, hkv, D
+    b.scale = 0.088
+    assert lib.gfx906_fa_decode_workspace_size(ctypes.byref(b)) > 0
