@@ -48,6 +48,7 @@ constexpr int NWC = 8;                      // compute warps (warpgroups 0, 1)
 constexpr int NTHREADS = 384;               // + warpgroup 2: warp 8 produces, 9-11 exit
 constexpr int MAXST = 4;                    // max pipeline slots (3 or 4 chosen per launch)
 constexpr int MAXP = 8;                     // max pages per stage
+constexpr int MAXG = 8;                     // max page-slot groups (NWC / HG)
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*232 + 128*40
 constexpr int REG_COMPUTE = 232;
@@ -60,12 +61,11 @@ struct DecodeParams {
   int G;                  // query heads per kv head
   int HG;                 // kv heads per CTA
   int HGN;                // head groups (num_heads_kv / HG)
-  int P;                  // pages per stage (= PPW * warps per head)
+  int NG;                 // page-slot groups per CTA (NWC / HG), each with its own item stream
+  int P;                  // pages per stage (= NG * PPW)
   int ppw;                // pages per compute warp per stage
   int CP;                 // pages per chunk (multiple of P)
   int S_max;              // chunks per sequence (upper bound)
-  int wph;                // compute warps per kv head (they split a chunk's pages)
-  int S_part;             // partial results per (sequence, kv head): S_max * wph
   int n_items;
   int R_pad;              // 16 * MT
   int rb_k, rb_v;         // bytes of one K / V row
@@ -73,6 +73,8 @@ struct DecodeParams {
   int vrec_contig;        // 1: the records of a CTA's kv heads are adjacent (one copy per page)
   int kgs, vgs;           // smem bytes per K group (4 tokens) / V group (2 tokens), padded to odd x 16
   int contig;             // 1: rows of consecutive tokens are adjacent (one copy per group)
+  int kwhole;             // 1: a page's K rows are one copy into an unpadded shared-memory page
+  int cps_log2;           // log2 of the producer's copy slots per page (2..32 slots)
   int kpage, vpage;       // smem bytes per page
   int stage_bytes;
   int q_off;              // smem offset of the Q tiles (MT == 2)
@@ -80,13 +82,17 @@ struct DecodeParams {
   int nst;                // pipeline slots of this launch
   float scale_log2;
   unsigned int* counter;  // work-queue counter (zeroed before the launch)
-  float* opart;           // [B][Hkv][S_part][R_pad][D]
-  float2* ml;             // [B][Hkv][S_part][R_pad]
+  float* opart;           // [B][Hkv][S_max][R_pad][D]
+  float2* ml;             // [B][Hkv][S_max][R_pad]
 };
 
+// Per stage and page-slot group (the HG warps g*HG .. g*HG+HG-1 that share
+// one item): the group's item (-1: no work in this stage), its first page,
+// valid pages, whether the item ends here; per page slot: copy issued.
 struct StageMeta {
-  int item, page0, npages, last;
+  int item[dec::MAXG], page0[dec::MAXG], npages[dec::MAXG], last[dec::MAXG];
   int ok[dec::MAXP];
+  int done;                               // terminator: every group's stream has ended
 };
 
 __device__ __forceinline__ void decode_item(const DecodeParams& d, int item, int& b, int& z, int& s) {
@@ -112,9 +118,6 @@ __device__ __forceinline__ bool item_pages(const DecodeParams& d, int b, int s, 
   return true;
 }
 
-__device__ __forceinline__ void named_sync_compute() {
-  asm volatile("bar.sync 1, %0;" ::"n"(dec::NWC * 32) : "memory");
-}
 
 // MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0 rows,
 // 3 Q8_0 page-transposed records).
@@ -155,83 +158,97 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     const int hgb_k = d.HG * d.rb_k, hgb_v = d.HG * d.rb_v;
     const uint32_t kbytes_page = (uint32_t)(PAGE * hgb_k);
     const uint32_t vbytes_page = (uint32_t)(PAGE * hgb_v);
-    constexpr int kCopies = 2 * PAGE;        // copy slots per page (12 used with adjacent rows, 32 without)
-    // items are claimed dynamically, so CTAs that drew short chunks take more
+    // copy slots per page, a power of two >= the copies a page needs, so a
+    // loop iteration of the warp issues the copies of 32 / slots pages
+    const int cps_log2 = d.cps_log2, kCopies = 1 << cps_log2;
+    // Lane g < NG holds group g's stream: its item and the next page to copy.
+    // Items are claimed dynamically, so streams that drew short chunks take
+    // more; a claim skips items without work (chunks past a sequence's end).
+    int g_item = -1, g_b = 0, g_h0 = 0, g_pg = 0, g_pe = 0;
+    bool g_active = false, g_exhausted = lane >= d.NG;
     while (alive) {
-      int item = 0;
-      if (lane == 0) item = (int)atomicAdd(d.counter, 1u);
-      item = __shfl_sync(0xffffffffu, item, 0);
-      if (item >= d.n_items) break;
-      int b, z, s, pb, pe, nsplit;
-      decode_item(d, item, b, z, s);
-      if (!item_pages(d, b, s, pb, pe, nsplit)) continue;
-      const int h0 = z * d.HG;
-      // block-table entries are read one stage ahead, so their latency hides
-      // behind the previous stage's copies and the empty-slot wait
-      int phys_next = -1;
-      if (lane < min(d.P, pe - pb)) phys_next = p.block_table[(int64_t)b * p.max_blocks + pb + lane];
-      for (int pg = pb;; pg += d.P) {
-        const int slot = it % NST;
-        const int phys = phys_next;
-        const int npg = max(0, min(d.P, pe - pg));
-        phys_next = -1;
-        if (lane < min(d.P, pe - pg - d.P)) phys_next = p.block_table[(int64_t)b * p.max_blocks + pg + d.P + lane];
-        if (it >= NST && !mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) { alive = false; break; }
-        const bool ok = lane < npg && phys >= 0;
-        if (lane < npg && phys < 0) raise_error(ERR_BAD_PAGE);
-        if (lane < MAXP) meta[slot].ok[lane] = ok ? 1 : 0;
-        const unsigned okmask = __ballot_sync(0xffffffffu, ok);
-        const bool last = pg + d.P >= pe;
-        if (lane == 0) {
-          meta[slot].item = item;
-          meta[slot].page0 = pg;
-          meta[slot].npages = npg;
-          meta[slot].last = last ? 1 : 0;
+      if (!g_active && !g_exhausted) {
+        for (;;) {
+          const int item = (int)atomicAdd(d.counter, 1u);
+          if (item >= d.n_items) { g_exhausted = true; break; }
+          int b, z, s, pb, pe, nsplit;
+          decode_item(d, item, b, z, s);
+          if (!item_pages(d, b, s, pb, pe, nsplit)) continue;
+          g_item = item; g_b = b; g_h0 = z * d.HG; g_pg = pb; g_pe = pe; g_active = true;
+          break;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], __popc(okmask) * (kbytes_page + vbytes_page));
-        __syncwarp();
-        uint8_t* kdst0 = smem + slot * d.stage_bytes;
-        uint8_t* vdst0 = kdst0 + d.P * d.kpage;
-        // uniform trip count for the whole warp (the shuffle needs every lane)
-        for (int c0 = 0; c0 < d.P * kCopies; c0 += 32) {
-          const int c = c0 + lane;
-          const int j = min(c / kCopies, MAXP - 1);
-          const int r = c - j * kCopies;
-          const int phys_j = __shfl_sync(0xffffffffu, phys, j);
-          if (c >= d.P * kCopies || j >= npg || !((okmask >> j) & 1)) continue;
-          // K: 4 groups of 4 tokens, V: 8 groups of 2 tokens (slots 0-3 / 4-11
-          // as whole-group copies, or 0-15 / 16-31 token by token)
-          const int nkc = d.contig ? 4 : 16;
-          const bool isk = r < nkc;
-          const int q = isk ? r : r - nkc;
-          if constexpr (VT == 3) {
-            if (!isk) {
-              // one copy of the adjacent records of all HG heads, or one per head
-              if (q >= (d.vrec_contig ? 1 : d.HG)) continue;
-              bulk_g2s(vdst0 + j * d.vpage + q * d.vrec,
-                       p.v_cache + (int64_t)phys_j * p.v_page_stride + (int64_t)(h0 + q) * p.v_head_stride,
-                       d.vrec_contig ? d.HG * d.vrec : d.vrec, &full_bar[slot]);
-              continue;
-            }
-          }
-          if (!isk && q >= (d.contig ? 8 : 16)) continue;
-          const int hgb = isk ? hgb_k : hgb_v;
-          const int gt = isk ? 4 : 2;             // tokens per group
-          const uint8_t* src = (isk ? p.k_cache : p.v_cache) +
-                               (int64_t)phys_j * (isk ? p.k_page_stride : p.v_page_stride) +
-                               (int64_t)h0 * (isk ? p.k_head_stride : p.v_head_stride);
-          const int64_t ts = isk ? p.k_tok_stride : p.v_tok_stride;
-          uint8_t* base = isk ? kdst0 + j * d.kpage : vdst0 + j * d.vpage;
-          const int gs = isk ? d.kgs : d.vgs;
-          if (d.contig) {
-            bulk_g2s(base + q * gs, src + (int64_t)(gt * q) * ts, gt * hgb, &full_bar[slot]);
-          } else {                                // token rows of a group are not adjacent in HBM
-            bulk_g2s(base + (q / gt) * gs + (q % gt) * hgb, src + (int64_t)q * ts, hgb, &full_bar[slot]);
+      }
+      const unsigned active = __ballot_sync(0xffffffffu, g_active);
+      if (active == 0) break;
+      // page slot l = g*PPW + pp (lanes l < P): block-table lookups are issued
+      // before the empty-slot wait, which hides their latency
+      const int gl = min(lane / PPW, MAXG - 1), pp = lane % PPW;
+      const int s_b = __shfl_sync(0xffffffffu, g_b, gl);
+      const int s_pg = __shfl_sync(0xffffffffu, g_pg, gl);
+      const int s_pe = __shfl_sync(0xffffffffu, g_pe, gl);
+      const int page = s_pg + pp;
+      const bool pvalid = lane < d.P && ((active >> gl) & 1) && page < s_pe;
+      const int phys = pvalid ? p.block_table[(int64_t)s_b * p.max_blocks + page] : -1;
+      const int slot = it % NST;
+      if (it >= NST && !mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) { alive = false; break; }
+      const bool ok = pvalid && phys >= 0;
+      if (pvalid && phys < 0) raise_error(ERR_BAD_PAGE);
+      if (lane < MAXP) meta[slot].ok[lane] = ok ? 1 : 0;
+      if (lane < MAXG) {
+        meta[slot].item[lane] = g_active ? g_item : -1;
+        meta[slot].page0[lane] = g_pg;
+        meta[slot].npages[lane] = g_active ? max(0, min(PPW, g_pe - g_pg)) : 0;
+        meta[slot].last[lane] = (g_active && g_pg + PPW >= g_pe) ? 1 : 0;
+      }
+      if (lane == 0) meta[slot].done = 0;
+      const unsigned okmask = __ballot_sync(0xffffffffu, ok);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&full_bar[slot], __popc(okmask) * (kbytes_page + vbytes_page));
+      __syncwarp();
+      uint8_t* kdst0 = smem + slot * d.stage_bytes;
+      uint8_t* vdst0 = kdst0 + d.P * d.kpage;
+      // uniform trip count for the whole warp (the shuffles need every lane)
+      for (int c0 = 0; c0 < d.P * kCopies; c0 += 32) {
+        const int c = c0 + lane;
+        const int j = min(c >> cps_log2, MAXP - 1);
+        const int r = c - j * kCopies;
+        const int phys_j = __shfl_sync(0xffffffffu, phys, j);
+        const int h0 = __shfl_sync(0xffffffffu, g_h0, min(j / PPW, MAXG - 1));
+        if (c >= d.P * kCopies || !((okmask >> j) & 1)) continue;
+        // K: 4 groups of 4 tokens, V: 8 groups of 2 tokens (slots 0-3 / 4-11
+        // as whole-group copies, or 0-15 / 16-31 token by token)
+        const int nkc = d.kwhole ? 1 : (d.contig ? 4 : 16);
+        const bool isk = r < nkc;
+        const int q = isk ? r : r - nkc;
+        if constexpr (VT == 3) {
+          if (!isk) {
+            // one copy of the adjacent records of all HG heads, or one per head
+            if (q >= (d.vrec_contig ? 1 : d.HG)) continue;
+            bulk_g2s(vdst0 + j * d.vpage + q * d.vrec,
+                     p.v_cache + (int64_t)phys_j * p.v_page_stride + (int64_t)(h0 + q) * p.v_head_stride,
+                     d.vrec_contig ? d.HG * d.vrec : d.vrec, &full_bar[slot]);
+            continue;
           }
         }
-        ++it;
-        if (last) break;
+        if (!isk && q >= (d.contig ? 8 : 16)) continue;
+        const int hgb = isk ? hgb_k : hgb_v;
+        const int gt = isk ? (d.kwhole ? PAGE : 4) : 2;   // tokens per copy
+        const uint8_t* src = (isk ? p.k_cache : p.v_cache) +
+                             (int64_t)phys_j * (isk ? p.k_page_stride : p.v_page_stride) +
+                             (int64_t)h0 * (isk ? p.k_head_stride : p.v_head_stride);
+        const int64_t ts = isk ? p.k_tok_stride : p.v_tok_stride;
+        uint8_t* base = isk ? kdst0 + j * d.kpage : vdst0 + j * d.vpage;
+        const int gs = isk ? d.kgs : d.vgs;
+        if (d.contig) {
+          bulk_g2s(base + q * gs, src + (int64_t)(gt * q) * ts, gt * hgb, &full_bar[slot]);
+        } else {                                // token rows of a group are not adjacent in HBM
+          bulk_g2s(base + (q / gt) * gs + (q % gt) * hgb, src + (int64_t)q * ts, hgb, &full_bar[slot]);
+        }
+      }
+      ++it;
+      if (g_active) {
+        g_pg += PPW;
+        if (g_pg >= g_pe) g_active = false;
       }
     }
     // terminator stage
@@ -239,7 +256,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
       const int slot = it % NST;
       if (it < NST || mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) {
         if (lane == 0) {
-          meta[slot].item = -1;
+          meta[slot].done = 1;
           mbar_arrive(&full_bar[slot]);
         }
       }
@@ -252,7 +269,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   // =========================================================================
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
   const int hl = warp % d.HG;       // local kv head
-  const int sub = warp / d.HG;      // page slot within a stage
+  const int sub = warp / d.HG;      // page-slot group: its own stream of items
   const int j4 = lane & 3;          // quad lane
   const int rq = lane >> 2;         // row within an 8-row group
 
@@ -281,14 +298,13 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   auto ld16 = [&](uint32_t a) { return *reinterpret_cast<const uint16_t*>(smem + (a - smem_base)); };
   auto ld8 = [&](uint32_t a) { return (uint32_t)*reinterpret_cast<const uint8_t*>(smem + (a - smem_base)); };
   auto ld64 = [&](uint32_t a) { return *reinterpret_cast<const uint2*>(smem + (a - smem_base)); };
-  const uint32_t qs_base = smem_base + d.q_off + hl * (MT * 16 * QROW);
+  const uint32_t qs_base = smem_base + d.q_off + warp * (MT * 16 * QROW);   // this warp's Q tile
 
   auto load_q = [&](int b, int h) {
     if constexpr (QS) {
-      // warps sharing a head write the same tile; sync before and after so no
-      // warp still reads the previous item's tile
-      named_sync_compute();
-      if (sub == 0) {
+      // each warp owns its tile (the groups switch items independently)
+      __syncwarp();
+      {
         for (int i = lane; i < MT * 16 * 64; i += 32) {   // 64 element pairs per row
           const int r = i >> 6, c = (i & 63) * 2;
           float x0 = 0.f, x1 = 0.f;
@@ -302,7 +318,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           asm volatile("st.shared.u32 [%0], %1;" ::"r"(qs_base + r * QROW + c * 2), "r"(v));
         }
       }
-      named_sync_compute();
+      __syncwarp();
     } else {
       // all loads of both rows are issued before any conversion, so the
       // item switch costs one memory latency instead of one per element
@@ -377,8 +393,6 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         v += __shfl_xor_sync(0xffffffffu, v, 2);
         lrow[mt][hh] = v;
       }
-    // every warp of a head writes its own partial result (the warps split the
-    // chunk's pages); decode_combine_kernel merges them with the other chunks'
     const int h = cz * d.HG + hl;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
@@ -388,7 +402,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
         if (r >= cR) continue;
         const float l = lrow[mt][hh];
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        if (cnsplit == 1 && d.wph == 1) {
+        if (cnsplit == 1) {
           const int t = r / d.G;
           const int hq = h * d.G + (r - t * d.G);
           const int64_t ob = o_offset(p, cb, t, hq);
@@ -397,7 +411,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
             store_out2(p.out, p.out_dtype, ob + nt * 8 + 2 * j4, o[mt][nt][hh * 2] * inv,
                        o[mt][nt][hh * 2 + 1] * inv);
         } else {
-          const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_part + cs * d.wph + sub) * d.R_pad + r;
+          const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_max + cs) * d.R_pad + r;
           float* op = d.opart + row * D;
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt)
@@ -412,12 +426,12 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   for (int it = 0;; ++it) {
     const int slot = it % NST;
     if (!mbar_wait(&full_bar[slot], (it / NST) & 1)) break;
-    const int item = meta[slot].item;
-    if (item < 0) break;
-    const int page0 = meta[slot].page0;
-    const int npages = meta[slot].npages;
-    const bool last = meta[slot].last != 0;
-    if (item != cur_item) {
+    if (meta[slot].done) break;
+    const int item = meta[slot].item[sub];        // -1: this warp's group has no work in the stage
+    const int page0 = meta[slot].page0[sub];
+    const int npages = meta[slot].npages[sub];
+    const bool last = meta[slot].last[sub] != 0;
+    if (item >= 0 && item != cur_item) {
       cur_item = item;
       decode_item(d, item, cb, cz, cs);
       cnq = seq_nq(p, cb);
@@ -438,7 +452,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
 #pragma unroll
     for (int pp = PPW - 1; pp >= 0; --pp) {
       const int s = sub * PPW + pp;
-      pok[pp] = s < npages && meta[slot].ok[s];
+      pok[pp] = item >= 0 && pp < npages && meta[slot].ok[s];
       if (pok[pp]) first_ok = pp;
     }
     if (first_ok >= 0) {
@@ -518,7 +532,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
           if (r >= cR) kv_lim = -1;
 #pragma unroll
           for (int pp = 0; pp < PPW; ++pp) {
-            const int k0 = (page0 + sub * PPW + pp) * PAGE;
+            const int k0 = (page0 + pp) * PAGE;
             // pages every row sees completely need no per-element mask
             const bool page_full = !MASK && pok[pp] && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1);
 #pragma unroll
@@ -681,7 +695,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[slot]);
-    if (last) epilogue();
+    if (item >= 0 && last) epilogue();
   }
 }
 
@@ -703,13 +717,13 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   if (nq <= 0 || nq * d.G > d.max_rows) return;
   const int kv_end = seq_kv_end(p, b, nq);
   const int npg = (kv_end + dec::PAGE - 1) / dec::PAGE;
-  const int nsplit = (npg == 0 ? 1 : (npg + d.CP - 1) / d.CP) * d.wph;   // partials of this sequence
+  const int nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;   // partials (chunks) of this sequence
   if (nsplit <= 1) return;
   const int R = nq * d.G;
   const int r = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (r >= R) return;
-  const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_part) * d.R_pad + r;
+  const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_max) * d.R_pad + r;
   float M = -INFINITY;
   for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
 #pragma unroll
@@ -783,7 +797,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   if (Hkv > 8 && d.HG != 8) return cudaErrorInvalidValue;
   d.HGN = Hkv / d.HG;
   d.ppw = 1;
-  d.P = NWC / d.HG;
+  d.P = NWC / d.HG;                        // one page per group per stage (PPW = 1)
   d.rb_k = q8_row_bytes(D);
   const bool vq8t = p.v_fmt == G9_VFMT_Q8T;
   d.rb_v = (p.v_fmt == G9_VFMT_Q8 || vq8t) ? q8_row_bytes(D) : 2 * D;
@@ -812,13 +826,28 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     if (!vq8t && (hgv % 16 || p.v_tok_stride % 16)) return cudaErrorInvalidValue;
   }
   d.kgs = pad_odd16(4 * hgk);
+  // One or two kv heads per CTA: the copy-request rate of the producer is the
+  // bound (per request cost, not bytes), so a page's K rows (adjacent in HBM)
+  // are copied whole into an unpadded page.  For these row sizes the padded
+  // 4-token groups do not remove bank conflicts anyway (1.5 / 2 wavefronts
+  // per fragment load either way); at 4 and 8 heads the padding halves or
+  // removes them and the rows are copied in 4-token groups.
+  d.kwhole = d.contig && d.HG <= 2;
+  if (d.kwhole) d.kgs = 4 * hgk;
+  {
+    const int kc = d.kwhole ? 1 : (d.contig ? 4 : 16);
+    const int vc = vq8t ? (d.vrec_contig ? 1 : d.HG) : (d.contig ? 8 : 16);
+    int l = 1;
+    while ((1 << l) < kc + vc) ++l;
+    d.cps_log2 = l;                       // 2 .. 32 slots
+  }
   d.vgs = pad_odd16(2 * hgv);
   d.kpage = (PAGE / 4) * d.kgs;
   // page-transposed V: the HG records back to back (ldmatrix rows are 16
   // consecutive bytes, conflict-free at any 16-byte aligned base)
   d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
-  d.wph = NWC / d.HG;
-  const int q_bytes = mt == 2 ? d.HG * mt * 16 * QROW : 0;
+  d.NG = NWC / d.HG;
+  const int q_bytes = mt == 2 ? NWC * mt * 16 * QROW : 0;   // one Q tile per compute warp
   constexpr int64_t kSmem = 227 * 1024;
   auto need = [&](int nst, int pages) {
     return (int64_t)nst * pages * (d.kpage + d.vpage) + q_bytes;
@@ -842,27 +871,27 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   const int sms = num_sms();
   const int max_pages = (p.max_kv + PAGE - 1) / PAGE;
   const int64_t est_pages = (int64_t)p.num_seqs * d.HGN * max_pages / 2 + 1;   // lengths ~ U[0, max]
-  const int64_t want = est_pages / ((int64_t)sms * 6);
+  const int64_t want = est_pages / ((int64_t)sms * d.NG * 6);   // items per group stream
   int cp = (int)std::min<int64_t>(std::max<int64_t>(want, 16), 512);
   // at most kCombineMaxParts partials per (sequence, kv head)
-  cp = std::max<int>(cp, (int)(((int64_t)max_pages * d.wph + kCombineMaxParts - 1) / kCombineMaxParts));
+  cp = std::max<int>(cp, (int)(((int64_t)max_pages + kCombineMaxParts - 1) / kCombineMaxParts));
   cp = ((cp + d.P - 1) / d.P) * d.P;
   d.CP = cp;
   d.S_max = max_pages == 0 ? 1 : (max_pages + cp - 1) / cp;
-  d.S_part = d.S_max * d.wph;
   d.n_items = p.num_seqs * d.HGN * d.S_max;
   return cudaSuccess;
 }
 
 static size_t decode_ws_bytes(const DecodeParams& d) {
-  const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_part * d.R_pad;
+  const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
   const size_t o = rows * dec::D * sizeof(float);
   return 256 + ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
 }
 
 template <int MT, int VT, bool MASK>
 static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
-  const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)d.HG * MT * 16 * dec::QROW : 0);
+  // one Q tile per compute warp (MT == 2)
+  const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)dec::NWC * MT * 16 * dec::QROW : 0);
   auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4, 1> : decode_kernel<MT, VT, MASK, 3, 1>;
   if constexpr (MT == 1) {
     if (d.ppw == 2) kern = decode_kernel<MT, VT, MASK, 3, 2>;
@@ -873,7 +902,7 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   kern<<<grid, dec::NTHREADS, smem, stream>>>(d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (d.S_part > 1) {
+  if (d.S_max > 1) {
     decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows, 0, stream>>>(d);
     e = cudaGetLastError();
   }
@@ -905,7 +934,7 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
   if (!workspace || workspace_bytes < decode_ws_bytes(d) || ((uintptr_t)workspace & 15)) return cudaErrorInvalidValue;
   {
     // [0, 256): work-queue counter; then partial O and (max, sum) rows
-    const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_part * d.R_pad;
+    const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
     uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
     d.counter = reinterpret_cast<unsigned int*>(w);
     d.opart = reinterpret_cast<float*>(w + 256);
