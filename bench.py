@@ -110,8 +110,8 @@ class ClockSampler:
 def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
     """Paged Q8_0 K + V cache for sequences of `lens` tokens, shuffled pages,
     filled by the fused store kernel from N(0,1) fp16 K/V.  v_fmt: "fp16",
-    "q8_0" (page-transposed Q8_0 records, the backend's layout) or
-    "q8_0rows" (Q8_0 token rows)."""
+    "q8_0" (page-transposed Q8_0 records) -- both in the backend's vLLM-shaped
+    allocation -- or "q8_0rows" (Q8_0 token rows in separate tensors)."""
     import torch
     import gfx906_fa
     g = torch.Generator(device=device).manual_seed(seed)
@@ -124,13 +124,15 @@ def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
     for b, n in enumerate(npg):
         bt[b, :n] = perm[c:c + n]
         c += n
-    k_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
-    if v_fmt == "q8_0":
-        v_cache = torch.zeros((NB, hkv, BS * RB), dtype=torch.uint8, device=device)
-    elif v_fmt == "q8_0rows":
+    if v_fmt == "q8_0rows":
+        k_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
         v_cache = torch.zeros((NB, BS, hkv, RB), dtype=torch.uint8, device=device)
     else:
-        v_cache = torch.zeros((NB, BS, hkv, D), dtype=torch.float16, device=device)
+        # the backend's own layout: one vLLM allocation [NB, 2, bs, Hkv, D] with
+        # Q8_0 K rows (and page-transposed Q8_0 V records) at each page's start
+        from gfx906_fa_paged import kv_cache_views
+        kv = torch.zeros((NB, 2, BS, hkv, D), dtype=torch.float16, device=device)
+        k_cache, v_cache = kv_cache_views(kv, v_fmt)
     chunk = 1 << 16
     for b, L in enumerate(lens):
         for t0 in range(0, int(L), chunk):

@@ -58,30 +58,7 @@ logger = init_logger(__name__)
 _V_FMT = _os.environ.get("GFX906_FA_V_FMT", "fp16").lower()
 
 
-def q8_row_bytes(head_size: int) -> int:
-    return (head_size // 32) * 34
-
-
-def kv_cache_views(kv_cache: torch.Tensor, v_fmt: str = "fp16"):
-    """Views of one vLLM KV allocation [NB, 2, bs, Hkv, D] (16-bit):
-
-    k_q8: uint8 [NB, bs, Hkv, D/32*34] -- dense Q8_0 rows at the start of
-          each page's K half;
-    v:    the V half [NB, bs, Hkv, D] (fp16 mode) or uint8
-          [NB, Hkv, bs*D/32*34] page-transposed Q8_0 records at the start of
-          each page's V half (q8_0): per kv head the fp16 block scales
-          [D/32][bs], then the int8 values [D][bs].
-    """
-    NB, two, bs, Hkv, D = kv_cache.shape
-    rb = q8_row_bytes(D)
-    page = bs * Hkv * D * kv_cache.element_size()
-    raw = kv_cache.view(torch.uint8).view(NB, 2, page)
-    k_q8 = raw[:, 0, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
-    if v_fmt == "q8_0":
-        v = raw[:, 1, :bs * Hkv * rb].view(NB, Hkv, bs * rb)
-    else:
-        v = kv_cache[:, 1]
-    return k_q8, v
+from gfx906_fa_paged import kv_cache_views, q8_row_bytes  # noqa: E402,F401  (cache layout)
 
 
 # -----------------------------------------------------------------------------

@@ -41,6 +41,35 @@ _DIRECT_PAGED_MIN_BATCH = int(_os.environ.get("GFX906_FA_DIRECT_PAGED_MIN_BATCH"
 _DIRECT_PAGED_MAX_SQ = int(_os.environ.get("GFX906_FA_DIRECT_PAGED_MAX_SQ", "16"))
 
 
+def q8_row_bytes(head_size: int) -> int:
+    return (head_size // 32) * 34
+
+
+def kv_cache_views(kv_cache: torch.Tensor, v_fmt: str = "fp16"):
+    """Views of one vLLM KV allocation [NB, 2, bs, Hkv, D] (16-bit), the
+    backend's cache layout:
+
+    k_q8: uint8 [NB, bs, Hkv, D/32*34] -- dense Q8_0 rows at the start of
+          each page;
+    v:    the V half [NB, bs, Hkv, D] (fp16 mode), or (q8_0) uint8
+          [NB, Hkv, bs*D/32*34] page-transposed Q8_0 records (per kv head the
+          fp16 block scales [D/32][bs], then the int8 values [D][bs]) placed
+          right after the K rows, so that a page's K and V are one contiguous
+          byte range (2*bs*Hkv*D/32*34 bytes, which fits the page's
+          2*bs*Hkv*D*2 bytes) and the decode kernel can fetch both with one
+          copy.
+    """
+    NB, two, bs, Hkv, D = kv_cache.shape
+    rb = q8_row_bytes(D)
+    raw = kv_cache.view(torch.uint8).view(NB, -1)
+    k_q8 = raw[:, :bs * Hkv * rb].view(NB, bs, Hkv, rb)
+    if v_fmt == "q8_0":
+        v = raw[:, bs * Hkv * rb:2 * bs * Hkv * rb].view(NB, Hkv, bs * rb)
+    else:
+        v = kv_cache[:, 1]
+    return k_q8, v
+
+
 def _should_use_direct_paged(num_seqs: int, max_seqlen_q: int) -> bool:
     """Path choice (reference: gfx906_fa_paged.py:60-70).  Only an explicit
     GFX906_FA_DIRECT_PAGED=0 selects the gather path."""

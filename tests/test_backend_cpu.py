@@ -65,11 +65,12 @@ def test_kv_cache_views_layout():
     assert v.data_ptr() == kv[:, 1].data_ptr()
     k2, v2 = be.kv_cache_views(kv, "q8_0")
     # page-transposed Q8_0 V: one record of 16*136 bytes per (page, kv head),
-    # at the start of each page's V half
+    # right after the page's K rows (K and V of a page are one byte range)
     assert v2.dtype == torch.uint8 and tuple(v2.shape) == (3, 8, 16 * 136)
     assert v2.stride() == (2 * 16 * 8 * 256, 16 * 136, 1)
+    assert v2.data_ptr() == k2.data_ptr() + 16 * 8 * 136
     v2[2, 1, 0] = 9
-    assert kv.view(torch.uint8).view(3, 2, -1)[2, 1, 16 * 136] == 9
+    assert kv.view(torch.uint8).view(3, -1)[2, 16 * 8 * 136 + 16 * 136] == 9
 
 
 def test_entry_point_declared():

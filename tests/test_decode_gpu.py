@@ -12,6 +12,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle as O
 from _paged import PagedCase, assert_close
 from _util import to_np
 
@@ -170,3 +171,42 @@ def test_config3_decode_full_size_subset_checked():
 
 def test_no_device_error_flagged():
     assert _gfx().device_error(True) == 0
+
+
+@pytest.mark.parametrize("hkv", [1, 2, 8])
+def test_decode_backend_cache_layout(hkv):
+    """Decode over the backend's own cache: one vLLM allocation [NB, 2, bs,
+    Hkv, D] with Q8_0 K rows and page-transposed Q8_0 V records adjacent at
+    each page's start (one copy per page when a CTA holds all kv heads)."""
+    import gfx906_fa_paged as P
+    lens = [3000, 17, 1, 777]
+    B, bs, D = len(lens), 16, 128
+    npg = [(L + bs - 1) // bs for L in lens]
+    NB = sum(npg) + 5
+    g = torch.Generator().manual_seed(hkv)
+    perm = torch.randperm(NB, generator=g).to(torch.int32)
+    bt = torch.full((B, max(npg)), -1, dtype=torch.int32)
+    c = 0
+    for b, n in enumerate(npg):
+        bt[b, :n] = perm[c:c + n]
+        c += n
+    kv = torch.zeros((NB, 2, bs, hkv, D), dtype=torch.float16, device=dev)
+    k8, v8 = P.kv_cache_views(kv, "q8_0")
+    T = sum(lens)
+    key = torch.randn((T, hkv, D), generator=g).half()
+    val = torch.randn((T, hkv, D), generator=g).half()
+    seq_of = np.repeat(np.arange(B), lens)
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    tpos = np.arange(T) - starts[seq_of]
+    slots = torch.from_numpy(bt.numpy()[seq_of, tpos // bs].astype(np.int64) * bs + tpos % bs)
+    _gfx().store_kv(key.to(dev), val.to(dev), slots.to(dev), k8, v8, 3)
+    q = _q((B, 6 * hkv, 1, D), torch.bfloat16, seed=hkv)
+    sl = torch.tensor(lens, dtype=torch.int32)
+    out = _gfx().forward_paged_direct(q.to(dev), k8, v8, bt.to(dev), sl.to(dev), 1.0 / np.sqrt(D))
+    rb = D // 32 * 34
+    ref = O.attention_paged(*_qnp(q)[:1], _qnp(q)[1], np.zeros(B, np.int32), np.ones(B, np.int32),
+                            np.ascontiguousarray(to_np(k8)), np.ascontiguousarray(to_np(v8)), bt.numpy(),
+                            sl.numpy(), 1.0 / np.sqrt(D), hkv, v_fmt="q8t",
+                            v_strides=(hkv * bs * rb, 0, bs * rb), q_strides=(6 * hkv * D, D, D),
+                            out_shape=(B, 6 * hkv, 1, D), o_strides=(6 * hkv * D, D, D))
+    assert_close(to_np(out), ref, what=f"backend layout hkv={hkv}")
