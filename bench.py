@@ -58,6 +58,27 @@ def config3_lens(seed=3):
     return rng.integers(1024, 32769, size=64).astype(np.int64)
 
 
+def config5_batch(seed=5):
+    """Mixed serving batch (config 5): 32 decode sequences with contexts
+    U[16K, 100K], each verifying 4 speculative tokens (causal within the 4),
+    plus 2 prefill chunks of 4096 tokens at offsets 0 and 24K.  Returns
+    (kv_lens, n_q) per sequence."""
+    rng = np.random.default_rng(seed)
+    dec = rng.integers(16384, 100001, size=32).astype(np.int64)
+    kv = np.concatenate([dec, [4096, 24576 + 4096]])
+    nq = np.concatenate([np.full(32, 4), [4096, 4096]])
+    return kv, nq
+
+
+def config5_work(kv, nq, hkv, hq, v_row):
+    """Algorithmic bytes (every visible K/V row once, Q in, O out, block
+    table) and FLOPs (4*D per visible (query head, key) pair, causal)."""
+    byt = int(np.sum(kv)) * hkv * (RB + v_row) + int(np.sum(nq)) * hq * D * 4
+    byt += int(sum((int(L) + BS - 1) // BS for L in kv)) * 4
+    pairs = sum(int(n) * int(L) - int(n) * (int(n) - 1) // 2 for L, n in zip(kv, nq))
+    return byt, 4 * D * hq * pairs
+
+
 # ---------------------------------------------------------------------------
 # clocks sampling
 # ---------------------------------------------------------------------------
@@ -228,6 +249,7 @@ def main():
                     help="first N sequences of config 3 (profiling uses a smaller case)")
     ap.add_argument("--prefill-tokens", type=int, default=32768)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-mixed", action="store_true", help="skip the config-5 mixed-batch measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -424,6 +446,48 @@ def main():
                                 "peak_kind": f"{peak_kind} bf16 burst"},
                    "gpu_launches_per_step": 3 * len(chunks)}
 
+    # ---------------- mixed serving batch (config 5) -------------------------
+    mixed = None
+    if not args.no_mixed:
+        if prefill is not None:
+            del kc, vc, btp, qp, op
+        torch.cuda.empty_cache()
+        kv5, nq5 = config5_batch()
+        k5, v5, bt5 = build_cache(kv5, hkv, seed=4000 + rank, device=device, v_fmt=args.v_fmt)
+        T5 = int(np.sum(nq5))
+        q5 = torch.randn((T5, hq, D), generator=gq, device=device).to(torch.bfloat16)
+        o5 = torch.empty_like(q5)
+        sl5 = torch.tensor(kv5, dtype=torch.int32, device=device)
+        cu5 = torch.tensor(np.concatenate([[0], np.cumsum(nq5)]), dtype=torch.int32, device=device)
+        nq5_l, kv5_l = [int(x) for x in nq5], [int(x) for x in kv5]
+
+        def mixed_step():
+            gfx906_fa.paged_attention(q5, k5, v5, bt5, sl5, cu5, max(nq5_l), max(kv5_l), scale, out=o5,
+                                      query_lens_host=nq5_l, seq_lens_host=kv5_l)
+
+        for _ in range(max(3, args.warmup)):
+            mixed_step()
+        barrier()
+        m0, m1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        msteps = max(3, args.steps // 2)
+        m0.record()
+        for _ in range(msteps):
+            mixed_step()
+        m1.record()
+        barrier()
+        mms = max_over_ranks(m0.elapsed_time(m1)) / msteps
+        v_row5 = RB if args.v_fmt.startswith("q8_0") else 2 * D
+        b5, f5 = config5_work(kv5, nq5, hkv, hq, v_row5)
+        t_lb = b5 / (hbm_peak * 1e9) + f5 / (tf_peak * 1e12)
+        mixed = {"value": T5 / (mms * 1e-3), "unit": "query tokens/s (all heads)", "ms_per_step": mms,
+                 "workload": "config5: 32 decode seqs x 4 speculative tokens (ctx U[16K,100K]) + 2 prefill "
+                             "chunks of 4096 at offsets 0 and 24K, one paged_attention call",
+                 "bytes_per_gpu": b5, "flops_per_gpu": f5,
+                 "roofline": {"bound": "hbm+tensor (serial sum)", "lower_bound_ms": t_lb * 1e3,
+                              "frac": t_lb / (mms * 1e-3)}}
+        del k5, v5, bt5, q5, o5
+        torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _ = cpu_baseline(seconds_target=10.0, v_fmt=args.v_fmt)
@@ -454,6 +518,8 @@ def main():
         }
         if fp16v:
             line["decode_fp16_v"] = fp16v
+        if mixed:
+            line["mixed_config5"] = mixed
         if prefill:
             line["prefill"] = prefill
         if cpu:

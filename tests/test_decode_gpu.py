@@ -152,7 +152,8 @@ def test_paged_attention_varlen_inplace_cache():
                             case.scale)
     assert out.dtype == torch.bfloat16
     ref = case.oracle_varlen(to_np(q), "bf16", nq)
-    assert_close(to_np(out.float()), ref, atol=4e-3, rtol=1.2e-2, what="varlen")
+    # bf16 output: its rounding (<= 2^-9 relative) is inside the relative term
+    assert_close(to_np(out.float()), ref, what="varlen")
 
 
 def test_config3_decode_full_size_subset_checked():

@@ -56,8 +56,8 @@ def test_varlen_without_host_lengths():
     out = _gfx().paged_attention(q.to(dev), case.k_cache, case.v_cache, case.block_table.to(dev),
                                  torch.from_numpy(case.seq_lens).to(dev), _cu(nq).to(dev), max(nq), max(lens),
                                  case.scale)
-    assert_close(to_np(out.float()), case.oracle_varlen(to_np(q), "bf16", nq), atol=4e-3, rtol=1.2e-2,
-                 what="mixed")
+    # bf16 output: its rounding (<= 2^-9 relative) is inside the relative term
+    assert_close(to_np(out.float()), case.oracle_varlen(to_np(q), "bf16", nq), what="mixed")
 
 
 @pytest.mark.parametrize("v_fmt", ["q8", "q8t", "bf16"])
