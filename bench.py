@@ -250,6 +250,7 @@ def main():
     ap.add_argument("--prefill-tokens", type=int, default=32768)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-mixed", action="store_true", help="skip the config-5 mixed-batch measurement")
+    ap.add_argument("--no-kv", action="store_true", help="skip the config-2 KV store + gather measurement")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -488,6 +489,57 @@ def main():
         del k5, v5, bt5, q5, o5
         torch.cuda.empty_cache()
 
+    # ---------------- config 2: Q8_0 KV store + paged gather ----------------
+    kvio = None
+    if not args.no_kv:
+        torch.cuda.empty_cache()
+        S2, L2, NB2 = 16, 4096, 70000
+        T2 = S2 * L2
+        g2 = torch.Generator(device=device).manual_seed(6 + rank)
+        pool = torch.randperm(NB2, generator=g2, device=device).to(torch.int32)
+        bt2 = pool[:S2 * (L2 // BS)].view(S2, L2 // BS).contiguous()
+        tpos = torch.arange(L2, device=device)
+        slots2 = (bt2[:, tpos // BS].to(torch.int64) * BS + tpos % BS).reshape(-1)
+        def outl(x):   # 1% of the elements scaled x8
+            m = torch.rand(x.shape, generator=g2, device=device) < 0.01
+            return torch.where(m, x * 8, x)
+        key2 = outl(torch.randn((T2, hkv, D), generator=g2, device=device, dtype=torch.float16))
+        val2 = outl(torch.randn((T2, hkv, D), generator=g2, device=device, dtype=torch.float16))
+        # the reference's layout for this path: a contiguous Q8_0 K cache beside the fp16 V cache
+        k2v = torch.zeros((NB2, BS, hkv, RB), dtype=torch.uint8, device=device)
+        v2v = torch.zeros((NB2, BS, hkv, D), dtype=torch.float16, device=device)
+        sl2 = torch.full((S2,), L2, dtype=torch.int32, device=device)
+        kout = torch.empty((S2, hkv, L2, RB), dtype=torch.uint8, device=device)
+        vout = torch.empty((S2, hkv, L2, D), dtype=torch.float16, device=device)
+
+        def timed(fn, n):
+            for _ in range(3):
+                fn()
+            barrier()
+            a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(n):
+                fn()
+            b_.record()
+            barrier()
+            return max_over_ranks(a.elapsed_time(b_)) / n
+
+        st_ms = timed(lambda: gfx906_fa.store_kv(key2, val2, slots2, k2v, v2v, 1), max(5, args.steps))
+        ga_ms = timed(lambda: gfx906_fa.gather_paged_kv_q8(k2v, v2v, bt2, sl2, L2, k_out=kout, v_out=vout),
+                      max(5, args.steps))
+        st_b = T2 * hkv * (2 * D * 2 + RB + 2 * D) + T2 * 8       # K, V in; Q8_0 K, V out; slots
+        ga_b = 2 * T2 * hkv * (RB + 2 * D) + S2 * (L2 // BS) * 4  # pages in, dense rows out; block table
+        kvio = {"workload": "config2: 16 seqs x 4096 tokens, 8 kv heads (per GPU share), d128, block 16, "
+                            "fp16 K/V N(0,1) with 1% x8 outliers, pages drawn from a 70K-page pool",
+                "kv_store": {"value": st_b * world / (st_ms * 1e-3) / 1e9, "unit": "GB/s", "ms": st_ms,
+                             "frac_of_hbm": st_b / (st_ms * 1e-3) / 1e9 / hbm_peak,
+                             "op": "store_kv (K -> Q8_0, V copied), fused"},
+                "gather": {"value": ga_b * world / (ga_ms * 1e-3) / 1e9, "unit": "GB/s", "ms": ga_ms,
+                           "frac_of_hbm": ga_b / (ga_ms * 1e-3) / 1e9 / hbm_peak,
+                           "op": "gather_paged_kv_q8 (Q8_0 K + fp16 V pages -> dense BHSD)"}}
+        del k2v, v2v, key2, val2, kout, vout
+        torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu, _ = cpu_baseline(seconds_target=10.0, v_fmt=args.v_fmt)
@@ -520,6 +572,8 @@ def main():
             line["decode_fp16_v"] = fp16v
         if mixed:
             line["mixed_config5"] = mixed
+        if kvio:
+            line["kv_store_gather_config2"] = kvio
         if prefill:
             line["prefill"] = prefill
         if cpu:

@@ -42,6 +42,7 @@ struct StoreArgs {
   int k_store_w;                // widest aligned store for K rows (2, 4 or 8 bytes)
   int v_store_w;                // same for V rows
   int vec_ok_k, vec_ok_v;       // 1 when 4-element vector loads are aligned
+  int hkv_log2, bs_log2;        // fast path: log2 of Hkv and block size (powers of two)
 };
 
 constexpr int kWarps = 8;
@@ -163,6 +164,109 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_kernel(StoreArgs a) {
   }
 }
 
+// Fast path for head_dim 128, 16-bit K / V, aligned rows, V copied or
+// absent: each warp takes 4 rows per iteration and issues all their K and V
+// loads first (the general kernel above walks one row at a time, so every
+// row waited a full DRAM latency and little was in flight).  Lane l holds
+// elements 4l..4l+3 of a row, i.e. slot l%8 of 32-element block l/8; the
+// quantisation arithmetic is the general kernel's.  V rows go from
+// registers straight to the cache; the Q8_0 K rows are assembled in shared
+// memory so that they leave as aligned 8-byte stores.
+constexpr int kFastRows = 4;
+constexpr int kFastRowBytes = (128 / QK) * QBLOCK;       // 136
+
+__global__ void __launch_bounds__(kWarps * 32) q8_store_fast_kernel(StoreArgs a) {
+  __shared__ __align__(16) uint8_t stage_all[kWarps][kFastRows * kFastRowBytes];
+  uint8_t* stage = stage_all[warp_id()];
+  const int lane = lane_id();
+  const int64_t rows = (int64_t)a.T * a.Hkv;
+  const bool bf_k = a.key_dt == DT_BF16, bf_v = a.val_dt == DT_BF16;
+  (void)bf_v;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp_id()) * kFastRows; r0 < rows;
+       r0 += (int64_t)gridDim.x * kWarps * kFastRows) {
+    uint2 kraw[kFastRows], vraw[kFastRows];
+    int64_t kdst[kFastRows], vdst[kFastRows];   // byte offsets in the caches, -1: skip the row
+#pragma unroll
+    for (int i = 0; i < kFastRows; ++i) {
+      const uint32_t row = (uint32_t)(r0 + i);
+      const bool valid = r0 + i < rows;
+      const uint32_t t = row >> a.hkv_log2, h = row & ((1u << a.hkv_log2) - 1);
+      const int64_t s = valid ? (a.slot_mapping ? a.slot_mapping[t] : (int64_t)t) : -1;
+      if (s >= 0) {
+        const uint64_t s64 = (uint64_t)s;
+        const uint32_t blk = (uint32_t)(s64 >> a.bs_log2);
+        const uint32_t off = (uint32_t)s64 & ((1u << a.bs_log2) - 1);
+        // cache strides < 2^31 (checked by the launcher), the in-page part
+        // below one page stride: one 32x32->64 multiply per address
+        kdst[i] = (int64_t)((uint64_t)blk * (uint32_t)a.kc_blk + (off * (uint32_t)a.kc_tok + h * (uint32_t)a.kc_head));
+        vdst[i] = (int64_t)((uint64_t)blk * (uint32_t)a.vc_blk + (off * (uint32_t)a.vc_tok + h * (uint32_t)a.vc_head));
+      } else {
+        kdst[i] = vdst[i] = -1;
+      }
+      // contiguous [T, Hkv, 128] rows (checked by the launcher)
+      kraw[i] = valid ? *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a.key) + (size_t)row * 128 + 4 * lane)
+                      : make_uint2(0u, 0u);
+      vraw[i] = (valid && a.v_mode == G9_V_COPY16)
+                    ? *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(a.value) + (size_t)row * 128 + 4 * lane)
+                    : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < kFastRows; ++i) {
+      float v[4];
+      if (bf_k) {
+        v[0] = __uint_as_float(kraw[i].x << 16); v[1] = __uint_as_float(kraw[i].x & 0xffff0000u);
+        v[2] = __uint_as_float(kraw[i].y << 16); v[3] = __uint_as_float(kraw[i].y & 0xffff0000u);
+      } else {
+        const float2 x0 = __half22float2(*reinterpret_cast<const __half2*>(&kraw[i].x));
+        const float2 x1 = __half22float2(*reinterpret_cast<const __half2*>(&kraw[i].y));
+        v[0] = x0.x; v[1] = x0.y; v[2] = x1.x; v[3] = x1.y;
+      }
+      float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+      // amax / 127 correctly rounded without the IEEE division routine:
+      // y = amax * fl(1/127), then one FMA correction.  Checked exhaustively
+      // (exact rational arithmetic) for every finite fp16 and bf16 value,
+      // which are all the values amax can take here (16-bit inputs).
+      constexpr float kInv127 = 1.0f / 127.0f;
+      const float y127 = __fmul_rn(amax, kInv127);
+      const float dq = fmaf(fmaf(-y127, 127.0f, amax), kInv127, y127);
+      const float id = dq > 0.0f ? __frcp_rn(dq) : 0.0f;
+      // rint(v*id) clamped to [-128, 127] without the (quarter-rate)
+      // float->int conversion: the product is rounded to fp32 as in the
+      // reference, then adding 1.5*2^23 rounds it to an integer with ties to
+      // even (exactly rintf for |x| < 2^22) and leaves it in the low mantissa
+      // bits; the clamp is applied to the sum, and the int8 is its low byte.
+      // Identical to the general kernel for finite inputs.
+      constexpr float kMagic = 12582912.0f;
+      uint32_t rb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float r = __fadd_rn(__fmul_rn(v[e], id), kMagic);
+        r = fminf(fmaxf(r, kMagic - 128.0f), kMagic + 127.0f);
+        rb[e] = __float_as_uint(r);
+      }
+      const uint32_t packed = __byte_perm(__byte_perm(rb[0], rb[1], 0x0040), __byte_perm(rb[2], rb[3], 0x0040), 0x5410);
+      uint8_t* out = stage + i * kFastRowBytes + (lane >> 3) * QBLOCK;
+      uint16_t* o16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * (lane & 7));
+      o16[0] = (uint16_t)(packed & 0xffffu);
+      o16[1] = (uint16_t)(packed >> 16);
+      if ((lane & 7) == 0) *reinterpret_cast<uint16_t*>(out) = __half_as_ushort(__float2half_rn(dq));
+      if (a.v_mode == G9_V_COPY16 && vdst[i] >= 0)
+        *reinterpret_cast<uint2*>(a.v_cache + vdst[i] + 8 * lane) = vraw[i];
+    }
+    __syncwarp();
+    // each Q8_0 K row (17 x 8 bytes) leaves from lanes 0..16
+#pragma unroll
+    for (int i = 0; i < kFastRows; ++i)
+      if (lane < kFastRowBytes / 8 && kdst[i] >= 0)
+        reinterpret_cast<uint64_t*>(a.k_cache + kdst[i])[lane] =
+            reinterpret_cast<const uint64_t*>(stage + i * kFastRowBytes)[lane];
+    __syncwarp();
+  }
+}
+
 static int store_width(const void* base, int64_t a, int64_t b, int64_t c, int row_bytes) {
   uintptr_t m = (uintptr_t)base | (uintptr_t)a | (uintptr_t)b | (uintptr_t)c | (uintptr_t)row_bytes;
   if ((m & 7) == 0) return 8;
@@ -187,7 +291,23 @@ static int grid_for_rows(int64_t rows) {
 cudaError_t launch_store(const StoreArgs& a, cudaStream_t stream) {
   const int64_t rows = (int64_t)a.T * a.Hkv;
   if (rows == 0) return cudaSuccess;
-  q8_store_kernel<<<grid_for_rows(rows), kWarps * 32, 0, stream>>>(a);
+  auto pow2 = [](int64_t x) { return x > 0 && (x & (x - 1)) == 0; };
+  auto small = [](int64_t x) { return x >= 0 && x < 0x7fffffff; };
+  const bool fast = a.D == 128 && rows < 0x7fffffff && a.key_dt != DT_F32 && a.vec_ok_k && a.k_store_w == 8 &&
+                    pow2(a.Hkv) && pow2(a.bs) && a.key_tok == (int64_t)a.Hkv * 128 && a.key_head == 128 &&
+                    small(a.kc_blk) && small(a.kc_tok) && small(a.kc_head) &&
+                    (a.v_mode == G9_V_NONE ||
+                     (a.v_mode == G9_V_COPY16 && a.val_dt != DT_F32 && a.vec_ok_v && a.v_store_w == 8 &&
+                      a.val_tok == (int64_t)a.Hkv * 128 && a.val_head == 128 && small(a.vc_blk) &&
+                      small(a.vc_tok) && small(a.vc_head)));
+  if (fast) {
+    StoreArgs f = a;
+    f.hkv_log2 = __builtin_ctzll((unsigned long long)a.Hkv);
+    f.bs_log2 = __builtin_ctzll((unsigned long long)a.bs);
+    q8_store_fast_kernel<<<grid_for_rows((rows + kFastRows - 1) / kFastRows), kWarps * 32, 0, stream>>>(f);
+  } else {
+    q8_store_kernel<<<grid_for_rows(rows), kWarps * 32, 0, stream>>>(a);
+  }
   return cudaGetLastError();
 }
 
