@@ -815,13 +815,19 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
 // combine: merge the partial results (per chunk and per warp of a head) of
 // sequences with more than one
 // ---------------------------------------------------------------------------
-// One CTA per (kv head, sequence), one warp per query row (R <= 32 rows).
-// Lanes reduce the partials' maxima; then, 32 partials at a time, lane j
-// computes the weight l_s * 2^(m_s - M) of partial base + j, and every lane
-// accumulates 4 of the 128 output dims of each partial (weights broadcast by
-// shuffle, 16-byte loads).
+// One CTA per (kv head, sequence); each query row (R <= 32) gets W = 32 / R
+// warps (at most 4), which split the row's partials.  A warp reduces its
+// partials' maxima, then, 32 partials at a time, lane j computes the weight
+// l_s * 2^(m_s - M) of partial base + j and every lane accumulates 4 of the
+// 128 output dims (weights broadcast by shuffle, 16-byte loads).  The W
+// warps of a row then combine their maxima, sums and numerators through
+// shared memory.
 constexpr int kCombineMaxParts = 1024;
+constexpr int kCombineMaxW = 4;
 __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams d) {
+  __shared__ float cm[32];                    // per warp (rows x W <= 32): max
+  __shared__ float cl[32];                    // den (relative to that max)
+  __shared__ float4 cn[32][32];               // numerators, 4 dims per lane
   const G9AttnBatch& p = d.p;
   const int b = blockIdx.y;
   const int h = blockIdx.x;
@@ -832,26 +838,32 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   const int nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;   // partials (chunks) of this sequence
   if (nsplit <= 1) return;
   const int R = nq * d.G;
-  const int r = threadIdx.x >> 5;
+  const int W = blockDim.x / (32 * d.max_rows);         // warps per row (uniform)
+  const int warp = threadIdx.x >> 5;
+  const int r = warp / W, wi = warp - r * W;
   const int lane = threadIdx.x & 31;
-  if (r >= R) return;
-  const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_max) * d.R_pad + r;
+  const bool active = r < R;
+  // partial range of this warp: [s0, s1)
+  const int per = (nsplit + W - 1) / W;
+  const int s0 = min(nsplit, wi * per), s1 = min(nsplit, s0 + per);
+  const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_max) * d.R_pad + (active ? r : 0);
   float M = -INFINITY;
-  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
+  if (active)
+    for (int s = s0 + lane; s < s1; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float mu = M == -INFINITY ? 0.f : M;
   float den = 0.f;
   float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
   const float* op = d.opart + row0 * dec::D + 4 * lane;
-  for (int base = 0; base < nsplit; base += 32) {
+  for (int base = s0; active && base < s1; base += 32) {
     float w = 0.f;
-    if (base + lane < nsplit) {
+    if (base + lane < s1) {
       const float2 ml = d.ml[row0 + (int64_t)(base + lane) * d.R_pad];
       w = ml.y * fast_exp2(ml.x - mu);
     }
     den += w;
-    const int n = min(32, nsplit - base);          // warp-uniform
+    const int n = min(32, s1 - base);              // warp-uniform
 #pragma unroll 4
     for (int j = 0; j < n; ++j) {
       const float wj = __shfl_sync(0xffffffffu, w, j);
@@ -862,12 +874,31 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-  const float inv = den > 0.f ? 1.f / den : 0.f;
+  if (active) {
+    if (lane == 0) { cm[warp] = M; cl[warp] = den; }
+    cn[warp][lane] = num;
+  }
+  __syncthreads();
+  if (!active || wi != 0) return;
+  float Mt = -INFINITY;
+  for (int k = 0; k < W; ++k) Mt = fmaxf(Mt, cm[warp + k]);
+  const float mt = Mt == -INFINITY ? 0.f : Mt;
+  float dsum = 0.f;
+  float4 nsum = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < W; ++k) {
+    const float mk = cm[warp + k];
+    const float a = mk == -INFINITY ? 0.f : fast_exp2(mk - mt);
+    dsum += a * cl[warp + k];
+    const float4 v = cn[warp + k][lane];
+    nsum.x = fmaf(a, v.x, nsum.x); nsum.y = fmaf(a, v.y, nsum.y);
+    nsum.z = fmaf(a, v.z, nsum.z); nsum.w = fmaf(a, v.w, nsum.w);
+  }
+  const float inv = dsum > 0.f ? 1.f / dsum : 0.f;
   const int t = r / d.G;
   const int hq = h * d.G + (r - t * d.G);
   const int64_t off = o_offset(p, b, t, hq) + 4 * lane;
-  store_out2(p.out, p.out_dtype, off, num.x * inv, num.y * inv);
-  store_out2(p.out, p.out_dtype, off + 2, num.z * inv, num.w * inv);
+  store_out2(p.out, p.out_dtype, off, nsum.x * inv, nsum.y * inv);
+  store_out2(p.out, p.out_dtype, off + 2, nsum.z * inv, nsum.w * inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -1026,7 +1057,8 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (d.S_max > 1) {
-    decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows, 0, stream>>>(d);
+    const int cw = std::max(1, std::min(kCombineMaxW, 32 / d.max_rows));   // warps per row
+    decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows * cw, 0, stream>>>(d);
     e = cudaGetLastError();
   }
   return e;
