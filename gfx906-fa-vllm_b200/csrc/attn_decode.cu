@@ -36,6 +36,7 @@
 // visible key produce zeros.  Every mbarrier wait is bounded (common.cuh).
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #include "attn_common.cuh"
 
@@ -83,6 +84,8 @@ struct DecodeParams {
   int q_off;              // smem offset of the Q tiles (MT == 2)
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
   int nst;                // pipeline slots of this launch
+  int tr;                 // 1: transposed consumer (<= 8 rows, page-transposed Q8_0 V)
+  uint32_t tr_tab;        // transposed consumer: key order per quad (see decode_consumer_tr)
   float scale_log2;
   unsigned int* counter;  // work-queue counter (zeroed before the launch)
   float* opart;           // [B][Hkv][S_max][R_pad][D]
@@ -122,10 +125,369 @@ __device__ __forceinline__ bool item_pages(const DecodeParams& d, int b, int s, 
 }
 
 
+// ---------------------------------------------------------------------------
+// Transposed consumer (at most 8 query rows per kv head, page-transposed
+// Q8_0 V).  The query rows are the N = 8 side of m16n8k16 instead of padding
+// a 16-row M tile:
+//   S^T = K . Q^T   (A = 16 keys x 16 dims of K, B = 16 dims x 8 rows of Q)
+//   O^T += V^T . P^T (A = 16 dims x 16 keys of V, B = 16 keys x 8 rows of P)
+// so a page takes 8 + 8 MMAs instead of 16 + 16, a thread holds 4 scores per
+// page instead of 8, and O^T is 32 registers.
+//
+// Exact int8 -> fp16 without a subtraction: (0x64 << 8) | (b ^ 0x80) is
+// 1152 + b.  The K side starts each block's accumulator at -1152 * (sum of
+// the block's Q dims), which cancels the offset exactly in the algebra (the
+// same fp16 Q values enter both).  The V side runs one extra MMA per block
+// whose A operand is a row of ones: it accumulates sum_k (P s_v)[k] with the
+// same fp16 B fragment the value MMAs use, and the epilogue subtracts 1152
+// times it.  V's per-(key, block) scale is applied to P (two half2 products
+// per block) instead of to V.
+//
+// Key order: accumulator row (m-slot) s of S^T is key sigma(s); after the
+// in-register transpose (movmatrix) the same slot is k-slot s of the P.V
+// product, whose V^T fragment comes straight from ldmatrix rows of 16 keys:
+// thread j gets keys 4j .. 4j+3, and k-slots (2j, 2j+1) take two of them
+// ("lo"), (2j+8, 2j+9) the other two ("hi").  Which two go low is chosen per
+// quad on the host so that the K rows a warp reads in one instruction fall
+// in different shared-memory banks for the launch's K layout (tr_tab: per
+// quad q, bits 8q.. hold lo0, lo1, hi0, hi1 as 2-bit positions).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t r;
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(a));
+  return r;
+}
+
+// two int8 (low 16 bits of x, zero-extended) -> fp16x2 of 1152 + b
+__device__ __forceinline__ uint32_t i8x2_to_h2_biased(uint32_t x) {
+  return __byte_perm(x ^ 0x8080u, 0x64646464u, 0x5140);
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+constexpr float kRescaleLog2T = 6.0f;     // P <= 2^6: P * s_v stays finite in fp16 for any fp16 V
+
+template <bool MASK, int NST, int PPW>
+__device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_t* smem, uint64_t* full_bar,
+                                                   uint64_t* empty_bar, StageMeta* meta, int warp, int lane) {
+  using namespace dec;
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
+  const G9AttnBatch& p = d.p;
+  const int hl = warp % d.HG;       // local kv head
+  const int sub = warp / d.HG;      // page-slot group
+  const int j4 = lane & 3;
+  const int rq = lane >> 2;
+  // this lane's two K rows (m-slots rq and rq + 8) and its V byte selectors
+  const uint32_t tq = (d.tr_tab >> (8 * (rq >> 1))) & 0xffu;
+  const int tA = 4 * (rq >> 1) + (int)((tq >> (2 * (rq & 1))) & 3u);
+  const int tB = 4 * (rq >> 1) + (int)((tq >> (4 + 2 * (rq & 1))) & 3u);
+  const uint32_t tj = (d.tr_tab >> (8 * j4)) & 0xffu;
+  const uint32_t l0 = tj & 3u, l1 = (tj >> 2) & 3u, h0 = (tj >> 4) & 3u, h1 = (tj >> 6) & 3u;
+  const uint32_t sel_lo = l0 | 0x40u | (l1 << 8) | 0x4000u;
+  const uint32_t sel_hi = h0 | 0x40u | (h1 << 8) | 0x4000u;
+  const uint32_t ssel_lo = (2 * l0) | ((2 * l0 + 1) << 4) | ((2 * l1) << 8) | ((2 * l1 + 1) << 12);
+  const uint32_t ssel_hi = (2 * h0) | ((2 * h0 + 1) << 4) | ((2 * h1) << 8) | ((2 * h1 + 1) << 12);
+  const int hgb_k = d.HG * d.rb_k;
+  const uint32_t kofA = (uint32_t)((tA >> 2) * d.kgs + (tA & 3) * hgb_k + hl * d.rb_k);
+  const uint32_t kofB = (uint32_t)((tB >> 2) * d.kgs + (tB & 3) * hgb_k + hl * d.rb_k);
+
+  float o[8][4];           // O^T: m-tile mt = dims 16mt .. 16mt+15; columns = rows 2*j4, 2*j4+1
+  float corr[4];           // row `blk` of this tile: sum over keys of (P s_v) for block blk
+  uint32_t qb[8][2];       // Q^T B fragments per 16-dim k-step
+  float kc[4][2];          // -1152 * sum of block blk's Q dims, rows 2*j4, 2*j4+1
+  float mrow[2], lrow[2];
+  int cur_item = -1, cb = 0, cz = 0, cs = 0, cnq = 0, cR = 0, ckv = 0, cqabs = 0, cnsplit = 1;
+
+  const uint32_t smem_base = smem_u32(smem);
+  auto ld16 = [&](uint32_t a) { return (uint32_t)*reinterpret_cast<const uint16_t*>(smem + (a - smem_base)); };
+  auto ld64 = [&](uint32_t a) { return *reinterpret_cast<const uint2*>(smem + (a - smem_base)); };
+
+  auto start_item = [&](int b, int h) {
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[mt][c] = 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) corr[c] = 0.f;
+    mrow[0] = mrow[1] = -INFINITY;
+    lrow[0] = lrow[1] = 0.f;
+    // Q row rq: dims 16ks + 2*j4 (+1) and 16ks + 2*j4 + 8 (+9); all loads first
+    const bool v = rq < cR;
+    const int t = v ? rq / d.G : 0;
+    const int64_t base = v ? q_offset(p, b, t, h * d.G + (rq - t * d.G)) : 0;
+    float qf[16][2];
+    if (p.q_dtype == DT_F32) {
+      const float* q = reinterpret_cast<const float*>(p.q);
+      float2 x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        x[i] = v ? *reinterpret_cast<const float2*>(q + base + (i >> 1) * 16 + (i & 1) * 8 + 2 * j4)
+                 : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) { qf[i][0] = x[i].x; qf[i][1] = x[i].y; }
+    } else {
+      const uint16_t* q = reinterpret_cast<const uint16_t*>(p.q);
+      uint32_t x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        x[i] = v ? *reinterpret_cast<const uint32_t*>(q + base + (i >> 1) * 16 + (i & 1) * 8 + 2 * j4) : 0u;
+      const bool bf = p.q_dtype == DT_BF16;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (bf) {
+          qf[i][0] = __uint_as_float(x[i] << 16);
+          qf[i][1] = __uint_as_float(x[i] & 0xffff0000u);
+        } else {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x[i]));
+          qf[i][0] = f.x;
+          qf[i][1] = f.y;
+        }
+      }
+    }
+    float qs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t hq = pack_half2(qf[i][0], qf[i][1]);
+      qb[i >> 1][i & 1] = hq;
+      const float2 r = __half22float2(*reinterpret_cast<const __half2*>(&hq));   // the values the MMA sees
+      qs[i >> 2] += r.x + r.y;
+    }
+#pragma unroll
+    for (int blk = 0; blk < 4; ++blk) {
+      float s = qs[blk];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);       // row rq's block sum, on all 4 lanes of the quad
+      kc[blk][0] = -1152.f * __shfl_sync(0xffffffffu, s, 8 * j4);
+      kc[blk][1] = -1152.f * __shfl_sync(0xffffffffu, s, 8 * j4 + 4);
+    }
+  };
+
+  auto epilogue = [&]() {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float v = lrow[c];
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      lrow[c] = v;
+    }
+    float cv[4][2];
+#pragma unroll
+    for (int blk = 0; blk < 4; ++blk) {
+      cv[blk][0] = 1152.f * __shfl_sync(0xffffffffu, corr[0], 4 * blk + j4);
+      cv[blk][1] = 1152.f * __shfl_sync(0xffffffffu, corr[1], 4 * blk + j4);
+    }
+    const int h = cz * d.HG + hl;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const int r = 2 * j4 + c;
+      if (r >= cR) continue;
+      const float l = lrow[c];
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      if (cnsplit == 1) {
+        const int t = r / d.G;
+        const int hq = h * d.G + (r - t * d.G);
+        const int64_t ob = o_offset(p, cb, t, hq);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float x = (o[mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
+            const int64_t off = ob + mt * 16 + hh * 8 + rq;
+            if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = x;
+            else if (p.out_dtype == DT_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
+            else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
+          }
+      } else {
+        const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_max + cs) * d.R_pad + r;
+        float* op = d.opart + row * D;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) op[mt * 16 + hh * 8 + rq] = (o[mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
+        if (rq == 0) d.ml[row] = make_float2(mrow[c], l);
+      }
+    }
+  };
+
+  for (int it = 0;; ++it) {
+    const int slot = it % NST;
+    if (!mbar_wait(&full_bar[slot], (it / NST) & 1)) break;
+    if (meta[slot].done) break;
+    const int item = meta[slot].item[sub];
+    const int page0 = meta[slot].page0[sub];
+    const int npages = meta[slot].npages[sub];
+    const bool last = meta[slot].last[sub] != 0;
+    if (item >= 0 && item != cur_item) {
+      cur_item = item;
+      decode_item(d, item, cb, cz, cs);
+      cnq = seq_nq(p, cb);
+      cR = cnq * d.G;
+      ckv = p.kv_len[cb];
+      cqabs = p.q_abs ? p.q_abs[cb] : 0;
+      int pb, pe;
+      item_pages(d, cb, cs, pb, pe, cnsplit);
+      start_item(cb, cz * d.HG + hl);
+    }
+    bool pok[PPW];
+    int first_ok = -1;
+#pragma unroll
+    for (int pp = PPW - 1; pp >= 0; --pp) {
+      pok[pp] = item >= 0 && pp < npages && meta[slot].ok[sub * PPW + pp];
+      if (pok[pp]) first_ok = pp;
+    }
+    if (first_ok >= 0) {
+      int psrc[PPW];
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) psrc[pp] = sub * PPW + (pok[pp] ? pp : first_ok);
+      const uint32_t stage_base = smem_base + slot * d.stage_bytes;
+      // ---------------- S^T = K Q^T ------------------------------------------
+      float sacc[PPW][4];
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) {
+        const uint32_t kb = stage_base + psrc[pp] * d.kps;
+        const uint32_t rA = kb + kofA, rB = kb + kofB;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) sacc[pp][c] = 0.f;
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          const uint32_t cA = rA + blk * QBLOCK + 2 + 2 * j4, cB = rB + blk * QBLOCK + 2 + 2 * j4;
+          uint32_t a0[4], a1[4];
+          a0[0] = i8x2_to_h2_biased(ld16(cA));
+          a0[1] = i8x2_to_h2_biased(ld16(cB));
+          a0[2] = i8x2_to_h2_biased(ld16(cA + 8));
+          a0[3] = i8x2_to_h2_biased(ld16(cB + 8));
+          a1[0] = i8x2_to_h2_biased(ld16(cA + 16));
+          a1[1] = i8x2_to_h2_biased(ld16(cB + 16));
+          a1[2] = i8x2_to_h2_biased(ld16(cA + 24));
+          a1[3] = i8x2_to_h2_biased(ld16(cB + 24));
+          const float dA = half_bits_to_float((uint16_t)ld16(rA + blk * QBLOCK));
+          const float dB = half_bits_to_float((uint16_t)ld16(rB + blk * QBLOCK));
+          float acc[4] = {kc[blk][0], kc[blk][1], kc[blk][0], kc[blk][1]};
+          mma_f16_16816(acc, a0, qb[2 * blk]);
+          mma_f16_16816(acc, a1, qb[2 * blk + 1]);
+          sacc[pp][0] = fmaf(acc[0], dA, sacc[pp][0]);
+          sacc[pp][1] = fmaf(acc[1], dA, sacc[pp][1]);
+          sacc[pp][2] = fmaf(acc[2], dB, sacc[pp][2]);
+          sacc[pp][3] = fmaf(acc[3], dB, sacc[pp][3]);
+        }
+      }
+      // ---------------- mask + online softmax (base 2, lazy max) --------------
+      float tmx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int r = 2 * j4 + c;
+        const int t = r / d.G;
+        int kv_lim = ckv;
+        if (p.q_abs) kv_lim = min(kv_lim, cqabs + t + 1);
+        if (r >= cR) kv_lim = -1;
+#pragma unroll
+        for (int pp = 0; pp < PPW; ++pp) {
+          const int k0 = (page0 + pp) * PAGE;
+          const bool page_full = !MASK && pok[pp] && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1) &&
+                                 r < cR;
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            float x = sacc[pp][2 * hb + c] * d.scale_log2;
+            if (!page_full) {
+              const int k = k0 + (hb ? tB : tA);
+              if constexpr (MASK) {
+                if (pok[pp] && r < cR && k < ckv)
+                  x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                      (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+              }
+              x = (pok[pp] && k < kv_lim) ? x : -INFINITY;
+            }
+            sacc[pp][2 * hb + c] = x;
+            tmx[c] = fmaxf(tmx[c], x);
+          }
+        }
+      }
+      const bool grow = tmx[0] > mrow[0] + kRescaleLog2T || tmx[1] > mrow[1] + kRescaleLog2T;
+      if (__any_sync(0xffffffffu, grow)) {
+        float alpha[2];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float mx = tmx[c];
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          alpha[c] = 1.f;
+          if (mx > mrow[c] + kRescaleLog2T) {        // uniform over the lanes of this row
+            alpha[c] = fast_exp2(mrow[c] - mx);
+            mrow[c] = mx;
+            lrow[c] *= alpha[c];
+          }
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          o[mt][0] *= alpha[0]; o[mt][2] *= alpha[0];
+          o[mt][1] *= alpha[1]; o[mt][3] *= alpha[1];
+        }
+        corr[0] *= alpha[0]; corr[2] *= alpha[0];
+        corr[1] *= alpha[1]; corr[3] *= alpha[1];
+      }
+      uint32_t pb[PPW][2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float mu = mrow[c] == -INFINITY ? 0.f : mrow[c];
+        float ls = 0.f;
+#pragma unroll
+        for (int pp = 0; pp < PPW; ++pp)
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            const float pv = fast_exp2(sacc[pp][2 * hb + c] - mu);
+            sacc[pp][2 * hb + c] = pv;
+            ls += pv;
+          }
+        lrow[c] += ls;
+      }
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) {
+        pb[pp][0] = movmatrix_trans(pack_half2(sacc[pp][0], sacc[pp][1]));
+        pb[pp][1] = movmatrix_trans(pack_half2(sacc[pp][2], sacc[pp][3]));
+      }
+      // ---------------- O^T += V^T P^T ------------------------------------------
+      const uint32_t ones = 0x3c003c00u;
+#pragma unroll
+      for (int pp = 0; pp < PPW; ++pp) {
+        const uint32_t vrec = stage_base + d.vbase + psrc[pp] * d.vps + hl * d.vrec;
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          uint32_t r4[4];
+          ldmatrix_x4(r4, vrec + 2 * 4 * PAGE + (blk * 32 + lane) * PAGE);
+          const uint2 sc = ld64(vrec + blk * 2 * PAGE + 8 * j4);
+          const uint32_t bq[2] = {hmul2_u32(pb[pp][0], __byte_perm(sc.x, sc.y, ssel_lo)),
+                                  hmul2_u32(pb[pp][1], __byte_perm(sc.x, sc.y, ssel_hi))};
+          uint32_t w[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) w[m] = r4[m] ^ 0x80808080u;
+          const uint32_t av0[4] = {__byte_perm(w[0], 0x64646464u, sel_lo), __byte_perm(w[1], 0x64646464u, sel_lo),
+                                   __byte_perm(w[0], 0x64646464u, sel_hi), __byte_perm(w[1], 0x64646464u, sel_hi)};
+          const uint32_t av1[4] = {__byte_perm(w[2], 0x64646464u, sel_lo), __byte_perm(w[3], 0x64646464u, sel_lo),
+                                   __byte_perm(w[2], 0x64646464u, sel_hi), __byte_perm(w[3], 0x64646464u, sel_hi)};
+          mma_f16_16816(o[2 * blk], av0, bq);
+          mma_f16_16816(o[2 * blk + 1], av1, bq);
+          const uint32_t a1s = rq == blk ? ones : 0u;
+          const uint32_t aones[4] = {a1s, 0u, a1s, 0u};
+          mma_f16_16816(corr, aones, bq);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    if (item >= 0 && last) epilogue();
+  }
+}
+
 // MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0 rows,
 // 3 Q8_0 page-transposed records).
 // NST: shared-memory pipeline slots.  PPW: pages per compute warp per stage.
-template <int MT, int VT, bool MASK, int NST, int PPW>
+// TR: transposed consumer (MT 1, VT 3 only).
+template <int MT, int VT, bool MASK, int NST, int PPW, bool TR = false>
 __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodeParams d) {
   using namespace dec;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -379,6 +741,10 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   // =========================================================================
   // compute warps
   // =========================================================================
+  if constexpr (TR) {
+    static_assert(MT == 1 && VT == 3, "transposed consumer: one m-tile, page-transposed Q8_0 V");
+    decode_consumer_tr<MASK, NST, PPW>(d, smem, full_bar, empty_bar, meta, warp, lane);
+  } else {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
   const int hl = warp % d.HG;       // local kv head
   const int sub = warp / d.HG;      // page-slot group: its own stream of items
@@ -809,6 +1175,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
     if (lane == 0) mbar_arrive(&empty_bar[slot]);
     if (item >= 0 && last) epilogue();
   }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -916,6 +1283,83 @@ static int num_sms() {
   return sms;
 }
 
+// Key order of the transposed consumer: per quad of 4 keys, which two feed
+// k-slots (2j, 2j+1).  Chosen to minimise shared-memory wavefronts of the K
+// fragment loads (8 rows x 4 lanes per instruction, 2-byte loads) for the
+// launch's K row addresses.
+static uint32_t search_tr_table(int kgs, int hgb_k) {
+  using namespace dec;
+  auto kaddr = [&](int key) { return (key >> 2) * kgs + (key & 3) * hgb_k; };
+  static const int pairs[6][4] = {{0, 1, 2, 3}, {0, 2, 1, 3}, {0, 3, 1, 2}, {1, 2, 0, 3}, {1, 3, 0, 2}, {2, 3, 0, 1}};
+  auto wavefronts = [](const int* addr, int n) {   // 4-byte banks; same word is a broadcast
+    int words[32][32], cnt[32] = {0}, worst = 0;
+    for (int i = 0; i < n; ++i) {
+      const int w = addr[i] >> 2, b = w & 31;
+      bool seen = false;
+      for (int k = 0; k < cnt[b]; ++k) seen |= words[b][k] == w;
+      if (!seen) words[b][cnt[b]++] = w;
+      worst = std::max(worst, cnt[b]);
+    }
+    return worst;
+  };
+  uint32_t best = 0;
+  int best_cost = 1 << 30;
+  for (int c = 0; c < 6 * 6 * 6 * 6; ++c) {
+    int sel[4], cc = c;
+    for (int q = 0; q < 4; ++q) { sel[q] = cc % 6; cc /= 6; }
+    int cost = 0;
+    for (int half = 0; half < 2; ++half) {
+      int rows[8];
+      for (int rq = 0; rq < 8; ++rq) {
+        const int q = rq >> 1;
+        rows[rq] = kaddr(4 * q + pairs[sel[q]][2 * half + (rq & 1)]);
+      }
+      for (int blk = 0; blk < 4; ++blk) {
+        int a[32];
+        for (int i = 0; i < 4; ++i) {
+          for (int l = 0; l < 32; ++l) a[l] = rows[l >> 2] + blk * QBLOCK + 2 + 2 * (l & 3) + 8 * i;
+          cost += wavefronts(a, 32);
+        }
+        for (int l = 0; l < 32; ++l) a[l] = rows[l >> 2] + blk * QBLOCK;
+        cost += wavefronts(a, 32);
+      }
+    }
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = 0;
+      for (int q = 0; q < 4; ++q) {
+        const int* pr = pairs[sel[q]];
+        best |= (uint32_t)(pr[0] | (pr[1] << 2) | (pr[2] << 4) | (pr[3] << 6)) << (8 * q);
+      }
+    }
+  }
+  return best;
+}
+
+// The search depends only on the K row geometry; results are cached (a few
+// layouts per process).
+static uint32_t choose_tr_table(const DecodeParams& d) {
+  struct Entry { int kgs, hgb_k; uint32_t tab; };
+  static Entry cache[16];
+  static int n = 0;
+  static std::mutex mu;
+  const int hgb_k = d.HG * d.rb_k;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (cache[i].kgs == d.kgs && cache[i].hgb_k == hgb_k) return cache[i].tab;
+  const uint32_t tab = search_tr_table(d.kgs, hgb_k);
+  if (n < 16) cache[n++] = Entry{d.kgs, hgb_k, tab};
+  return tab;
+}
+
+static bool decode_tr_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("GFX906_FA_DECODE_TRANSPOSED");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // Fills DecodeParams from the batch; returns cudaErrorInvalidValue when the
 // batch is outside what the decode kernel handles.
 static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
@@ -1020,6 +1464,8 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     d.vbase = d.P * d.kpage;
   }
   d.q_off = d.nst * d.stage_bytes;
+  d.tr = vq8t && R <= 8 && decode_tr_enabled();
+  if (d.tr) d.tr_tab = choose_tr_table(d);
   d.scale_log2 = p.scale * kLog2e;
   // chunking: enough chunks to keep every SM busy several times over
   const int sms = num_sms();
@@ -1049,6 +1495,12 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4, 1> : decode_kernel<MT, VT, MASK, 3, 1>;
   if constexpr (MT == 1) {
     if (d.ppw == 2) kern = decode_kernel<MT, VT, MASK, 3, 2>;
+    if constexpr (VT == 3) {
+      if (d.tr) {
+        kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, true> : decode_kernel<1, 3, MASK, 3, 1, true>;
+        if (d.ppw == 2) kern = decode_kernel<1, 3, MASK, 3, 2, true>;
+      }
+    }
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
