@@ -48,8 +48,16 @@ constexpr int PAGE = 16;
 constexpr int NWC = 8;                      // compute warps (warpgroups 0, 1)
 constexpr int NTHREADS = 384;               // + warpgroup 2: warp 8 produces, 9-11 exit
 constexpr int MAXST = 4;                    // max pipeline slots (3 or 4 chosen per launch)
-constexpr int MAXP = 8;                     // max pages per stage
-constexpr int MAXG = 8;                     // max page-slot groups (NWC / HG)
+constexpr int MAXP = 16;                    // max pages per stage
+constexpr int MAXG = 16;                    // max page-slot groups (compute warps / HG)
+// Transposed consumer with one kv head per CTA: 16 compute warps + a
+// producer warpgroup (640 threads launched at 96 registers:
+// 16*32*104 + 4*32*64 = 640*96).  With more heads per CTA it runs with the
+// 8-warp geometry above (two pages per warp).
+constexpr int NWC_TR = 16;
+constexpr int NTHREADS_TR = 640;
+constexpr int REG_COMPUTE_TR = 104;
+constexpr int REG_PRODUCER_TR = 64;
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*224 + 128*56 (the producer's
 // per-group stream state needs 56 to stay out of local memory)
@@ -84,7 +92,7 @@ struct DecodeParams {
   int q_off;              // smem offset of the Q tiles (MT == 2)
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
   int nst;                // pipeline slots of this launch
-  int tr;                 // 1: transposed consumer (<= 8 rows, page-transposed Q8_0 V)
+  int tr;                 // 0, or compute warps of the transposed consumer (<= 8 rows, page-transposed Q8_0 V)
   uint32_t tr_tab;        // transposed consumer: key order per quad (see decode_consumer_tr)
   float scale_log2;
   unsigned int* counter;  // work-queue counter (zeroed before the launch)
@@ -163,6 +171,15 @@ __device__ __forceinline__ uint32_t i8x2_to_h2_biased(uint32_t x) {
   return __byte_perm(x ^ 0x8080u, 0x64646464u, 0x5140);
 }
 
+// d = a.b + c with the accumulator rows (c0, c1, c0, c1)
+__device__ __forceinline__ void mma_f16_16816_c(float d[4], const uint32_t a[4], const uint32_t b[2], float c0,
+                                                float c1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%10,%11};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]), "f"(c0), "f"(c1));
+}
+
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
@@ -170,11 +187,11 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 
 constexpr float kRescaleLog2T = 6.0f;     // P <= 2^6: P * s_v stays finite in fp16 for any fp16 V
 
-template <bool MASK, int NST, int PPW>
+template <bool MASK, int NST, int PPW, int NW>
 __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_t* smem, uint64_t* full_bar,
                                                    uint64_t* empty_bar, StageMeta* meta, int warp, int lane) {
   using namespace dec;
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(NW == NWC_TR ? REG_COMPUTE_TR : REG_COMPUTE));
   const G9AttnBatch& p = d.p;
   const int hl = warp % d.HG;       // local kv head
   const int sub = warp / d.HG;      // page-slot group
@@ -199,7 +216,11 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
   uint32_t qb[8][2];       // Q^T B fragments per 16-dim k-step
   float kc[4][2];          // -1152 * sum of block blk's Q dims, rows 2*j4, 2*j4+1
   float mrow[2], lrow[2];
-  int cur_item = -1, cb = 0, cz = 0, cs = 0, cnq = 0, cR = 0, ckv = 0, cqabs = 0, cnsplit = 1;
+  // item state kept live: rows, and per row of this thread (2*j4 + c) the
+  // exclusive end of its visible keys (-1 for a padding row); the rest is
+  // decoded from the item again at the epilogue
+  int cur_item = -1, cR = 0;
+  int klim[2] = {-1, -1};
 
   const uint32_t smem_base = smem_u32(smem);
   auto ld16 = [&](uint32_t a) { return (uint32_t)*reinterpret_cast<const uint16_t*>(smem + (a - smem_base)); };
@@ -266,6 +287,9 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
   };
 
   auto epilogue = [&]() {
+    int cb, cz, cs, pb_, pe_, cnsplit;
+    decode_item(d, cur_item, cb, cz, cs);
+    item_pages(d, cb, cs, pb_, pe_, cnsplit);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       float v = lrow[c];
@@ -323,13 +347,18 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
     const bool last = meta[slot].last[sub] != 0;
     if (item >= 0 && item != cur_item) {
       cur_item = item;
+      int cb, cz, cs;
       decode_item(d, item, cb, cz, cs);
-      cnq = seq_nq(p, cb);
-      cR = cnq * d.G;
-      ckv = p.kv_len[cb];
-      cqabs = p.q_abs ? p.q_abs[cb] : 0;
-      int pb, pe;
-      item_pages(d, cb, cs, pb, pe, cnsplit);
+      cR = seq_nq(p, cb) * d.G;
+      const int ckv = p.kv_len[cb];
+      const int cqabs = p.q_abs ? p.q_abs[cb] : 0;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int r = 2 * j4 + c;
+        int lim = ckv;
+        if (p.q_abs) lim = min(lim, cqabs + r / d.G + 1);
+        klim[c] = r < cR ? lim : -1;
+      }
       start_item(cb, cz * d.HG + hl);
     }
     bool pok[PPW];
@@ -366,8 +395,8 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
           a1[3] = i8x2_to_h2_biased(ld16(cB + 24));
           const float dA = half_bits_to_float((uint16_t)ld16(rA + blk * QBLOCK));
           const float dB = half_bits_to_float((uint16_t)ld16(rB + blk * QBLOCK));
-          float acc[4] = {kc[blk][0], kc[blk][1], kc[blk][0], kc[blk][1]};
-          mma_f16_16816(acc, a0, qb[2 * blk]);
+          float acc[4];
+          mma_f16_16816_c(acc, a0, qb[2 * blk], kc[blk][0], kc[blk][1]);
           mma_f16_16816(acc, a1, qb[2 * blk + 1]);
           sacc[pp][0] = fmaf(acc[0], dA, sacc[pp][0]);
           sacc[pp][1] = fmaf(acc[1], dA, sacc[pp][1]);
@@ -379,25 +408,24 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
       float tmx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        const int r = 2 * j4 + c;
-        const int t = r / d.G;
-        int kv_lim = ckv;
-        if (p.q_abs) kv_lim = min(kv_lim, cqabs + t + 1);
-        if (r >= cR) kv_lim = -1;
+        const int kv_lim = klim[c];
 #pragma unroll
         for (int pp = 0; pp < PPW; ++pp) {
           const int k0 = (page0 + pp) * PAGE;
-          const bool page_full = !MASK && pok[pp] && k0 + PAGE <= ckv && (!p.q_abs || k0 + PAGE <= cqabs + 1) &&
-                                 r < cR;
+          const bool page_full = !MASK && pok[pp] && k0 + PAGE <= kv_lim;
 #pragma unroll
           for (int hb = 0; hb < 2; ++hb) {
             float x = sacc[pp][2 * hb + c] * d.scale_log2;
             if (!page_full) {
               const int k = k0 + (hb ? tB : tA);
               if constexpr (MASK) {
-                if (pok[pp] && r < cR && k < ckv)
+                if (pok[pp] && k < kv_lim) {
+                  int cb, cz, cs;
+                  decode_item(d, cur_item, cb, cz, cs);
+                  const int t = (2 * j4 + c) / d.G;
                   x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
                       (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+                }
               }
               x = (pok[pp] && k < kv_lim) ? x : -INFINITY;
             }
@@ -486,9 +514,12 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
 // MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0 rows,
 // 3 Q8_0 page-transposed records).
 // NST: shared-memory pipeline slots.  PPW: pages per compute warp per stage.
-// TR: transposed consumer (MT 1, VT 3 only).
-template <int MT, int VT, bool MASK, int NST, int PPW, bool TR = false>
-__global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodeParams d) {
+// TRW: 0, or the compute warps (8 or 16) of the transposed consumer (MT 1,
+// VT 3 only).
+template <int MT, int VT, bool MASK, int NST, int PPW, int TRW = 0>
+__global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::NTHREADS, 1)
+    decode_kernel(const DecodeParams d) {
+  constexpr bool TR = TRW != 0;
   using namespace dec;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[NST];
@@ -498,6 +529,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   const int warp = warp_id();
   const int lane = lane_id();
   const G9AttnBatch& p = d.p;
+  constexpr int NWC = TR ? TRW : dec::NWC;   // compute warps; warp NWC produces
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NST; ++i) {
@@ -516,7 +548,8 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   // conflict-free for the tensor-core operand loads.
   // =========================================================================
   if (warp >= NWC) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
+    if constexpr (TRW == NWC_TR) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER_TR));
+    else asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_PRODUCER));
     if (warp != NWC) return;
     int it = 0;
     bool alive = true;
@@ -743,7 +776,7 @@ __global__ void __launch_bounds__(dec::NTHREADS, 1) decode_kernel(const DecodePa
   // =========================================================================
   if constexpr (TR) {
     static_assert(MT == 1 && VT == 3, "transposed consumer: one m-tile, page-transposed Q8_0 V");
-    decode_consumer_tr<MASK, NST, PPW>(d, smem, full_bar, empty_bar, meta, warp, lane);
+    decode_consumer_tr<MASK, NST, PPW, NWC>(d, smem, full_bar, empty_bar, meta, warp, lane);
   } else {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
   const int hl = warp % d.HG;       // local kv head
@@ -1433,7 +1466,10 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // page-transposed V: the HG records back to back (ldmatrix rows are 16
   // consecutive bytes, conflict-free at any 16-byte aligned base)
   d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
-  d.NG = NWC / d.HG;
+  d.tr = vq8t && R <= 8 && decode_tr_enabled() ? (d.HG == 1 ? NWC_TR : NWC) : 0;
+  const int nwc = d.tr ? d.tr : NWC;
+  d.P = nwc / d.HG;
+  d.NG = nwc / d.HG;
   const int q_bytes = mt == 2 ? NWC * mt * 16 * QROW : 0;   // one Q tile per compute warp
   constexpr int64_t kSmem = 227 * 1024;
   auto need = [&](int nst, int pages) {
@@ -1443,7 +1479,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
   // (one m-tile only: with two the registers would spill); else one page per
   // warp with 4 stages, or 3 when 4 do not fit.
-  if (mt == 1 && 2 * d.P <= MAXP && need(3, 2 * d.P) <= kSmem) {
+  if (d.tr != NWC_TR && mt == 1 && 2 * d.P <= 8 && need(3, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = 3;
@@ -1464,7 +1500,6 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     d.vbase = d.P * d.kpage;
   }
   d.q_off = d.nst * d.stage_bytes;
-  d.tr = vq8t && R <= 8 && decode_tr_enabled();
   if (d.tr) d.tr_tab = choose_tr_table(d);
   d.scale_log2 = p.scale * kLog2e;
   // chunking: enough chunks to keep every SM busy several times over
@@ -1496,16 +1531,18 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   if constexpr (MT == 1) {
     if (d.ppw == 2) kern = decode_kernel<MT, VT, MASK, 3, 2>;
     if constexpr (VT == 3) {
-      if (d.tr) {
-        kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, true> : decode_kernel<1, 3, MASK, 3, 1, true>;
-        if (d.ppw == 2) kern = decode_kernel<1, 3, MASK, 3, 2, true>;
+      if (d.tr == dec::NWC_TR) {
+        kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC_TR> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC_TR>;
+      } else if (d.tr) {
+        kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC>;
+        if (d.ppw == 2) kern = decode_kernel<1, 3, MASK, 3, 2, dec::NWC>;
       }
     }
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = std::max(1, std::min(d.n_items, num_sms()));
-  kern<<<grid, dec::NTHREADS, smem, stream>>>(d);
+  kern<<<grid, d.tr == dec::NWC_TR ? dec::NTHREADS_TR : dec::NTHREADS, smem, stream>>>(d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (d.S_max > 1) {
