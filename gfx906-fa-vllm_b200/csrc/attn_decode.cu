@@ -58,6 +58,7 @@ constexpr int NWC_TR = 16;
 constexpr int NTHREADS_TR = 640;
 constexpr int REG_COMPUTE_TR = 104;
 constexpr int REG_PRODUCER_TR = 64;
+constexpr int kMaxRanksTR = 4095;           // (sequence, head group) pairs: prefix sums in shared memory
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*224 + 128*56 (the producer's
 // per-group stream state needs 56 to stay out of local memory)
@@ -74,7 +75,7 @@ struct DecodeParams {
   int NG;                 // page-slot groups per CTA (NWC / HG), each with its own item stream
   int P;                  // pages per stage (= NG * PPW)
   int ppw;                // pages per compute warp per stage
-  int CP;                 // pages per chunk (multiple of P)
+  int CP;                 // pages per chunk (multiple of ppw)
   int S_max;              // chunks per sequence (upper bound)
   int n_items;
   int R_pad;              // 16 * MT
@@ -93,6 +94,14 @@ struct DecodeParams {
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
   int nst;                // pipeline slots of this launch
   int tr;                 // 0, or compute warps of the transposed consumer (<= 8 rows, page-transposed Q8_0 V)
+  // Balanced split (the transposed kernels): units = pages of each rank
+  // (sequence b, head group z; rank = b*HGN + z) in rank order; stream s of
+  // the nstreams = grid*NG item streams owns units [s*T/N, (s+1)*T/N),
+  // N = min(nstreams, T).  A stream's piece of one rank is a segment; its
+  // partial result goes to slot s + rank.
+  int nranks, nstreams;
+  int cpre_off;           // smem offset of the rank prefix sums (nranks + 1 ints)
+  int* cpre_g;            // the same prefix sums, written by CTA 0 for the combine
   uint32_t tr_tab;        // transposed consumer: key order per quad (see decode_consumer_tr)
   float scale_log2;
   unsigned int* counter;  // work-queue counter (zeroed before the launch)
@@ -160,6 +169,25 @@ __device__ __forceinline__ bool item_pages(const DecodeParams& d, int b, int s, 
 // in different shared-memory banks for the launch's K layout (tr_tab: per
 // quad q, bits 8q.. hold lo0, lo1, hi0, hi1 as 2-bit positions).
 // ---------------------------------------------------------------------------
+// Units of a rank: its pages, or one masked unit when its rows see no key
+// (so that its zero output is written); 0 for sequences this kernel skips.
+// `real` returns the pages that exist.
+__device__ __forceinline__ int rank_units(const DecodeParams& d, int rank, int& real) {
+  const int b = rank / d.HGN;
+  const int nq = seq_nq(d.p, b);
+  real = 0;
+  if (nq <= 0 || nq * d.G > d.max_rows) return 0;
+  real = (seq_kv_end(d.p, b, nq) + dec::PAGE - 1) / dec::PAGE;
+  return max(real, 1);
+}
+__device__ __forceinline__ int64_t bal_bound(int s, int64_t T, int N) { return (int64_t)s * T / N; }
+// stream owning unit u (0 <= u < T, N <= T so no stream is empty)
+__device__ __forceinline__ int bal_sid(int64_t u, int64_t T, int N) {
+  int s = (int)(u * N / T);
+  if (s + 1 < N && bal_bound(s + 1, T, N) <= u) ++s;
+  return s;
+}
+
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
   uint32_t r;
   asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(a));
@@ -286,10 +314,17 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
     }
   };
 
+  // balanced split: this warp's stream and the rank prefix sums
+  const int* cpre = reinterpret_cast<const int*>(smem + d.cpre_off);
+  const int sid = blockIdx.x * d.NG + sub;
+  const int64_t T = cpre[d.nranks];
+  const int NS = (int)(T < d.nstreams ? T : (int64_t)d.nstreams);
+
   auto epilogue = [&]() {
-    int cb, cz, cs, pb_, pe_, cnsplit;
-    decode_item(d, cur_item, cb, cz, cs);
-    item_pages(d, cb, cs, pb_, pe_, cnsplit);
+    const int rank = cur_item - sid;
+    const int cb = rank / d.HGN, cz = rank - cb * d.HGN;
+    // the stream holds the whole rank: final output, else a partial
+    const bool whole = cpre[rank] >= bal_bound(sid, T, NS) && cpre[rank + 1] <= bal_bound(sid + 1, T, NS);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       float v = lrow[c];
@@ -311,7 +346,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
       if (r >= cR) continue;
       const float l = lrow[c];
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      if (cnsplit == 1) {
+      if (whole) {
         const int t = r / d.G;
         const int hq = h * d.G + (r - t * d.G);
         const int64_t ob = o_offset(p, cb, t, hq);
@@ -326,7 +361,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
             else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
           }
       } else {
-        const int64_t row = (((int64_t)cb * p.num_heads_kv + h) * d.S_max + cs) * d.R_pad + r;
+        const int64_t row = ((int64_t)cur_item * d.HG + hl) * d.R_pad + r;
         float* op = d.opart + row * D;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt)
@@ -347,8 +382,8 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
     const bool last = meta[slot].last[sub] != 0;
     if (item >= 0 && item != cur_item) {
       cur_item = item;
-      int cb, cz, cs;
-      decode_item(d, item, cb, cz, cs);
+      const int rank = item - sid;
+      const int cb = rank / d.HGN, cz = rank - cb * d.HGN;
       cR = seq_nq(p, cb) * d.G;
       const int ckv = p.kv_len[cb];
       const int cqabs = p.q_abs ? p.q_abs[cb] : 0;
@@ -420,8 +455,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
               const int k = k0 + (hb ? tB : tA);
               if constexpr (MASK) {
                 if (pok[pp] && k < kv_lim) {
-                  int cb, cz, cs;
-                  decode_item(d, cur_item, cb, cz, cs);
+                  const int cb = (cur_item - sid) / d.HGN;
                   const int t = (2 * j4 + c) / d.G;
                   x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
                       (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
@@ -538,6 +572,32 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
     }
     fence_barrier_init();
   }
+  if constexpr (TR) {
+    // rank prefix sums (balanced split), one warp: contiguous ranks per lane
+    if (warp == 0) {
+      int* cpre = reinterpret_cast<int*>(smem + d.cpre_off);
+      const int n = d.nranks, per = (n + 31) / 32;
+      const int r0 = min(n, lane * per), r1 = min(n, r0 + per);
+      int sum = 0, real;
+      for (int r = r0; r < r1; ++r) sum += rank_units(d, r, real);
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      int run = incl - sum;
+      for (int r = r0; r < r1; ++r) {
+        cpre[r] = run;
+        if (blockIdx.x == 0) d.cpre_g[r] = run;
+        run += rank_units(d, r, real);
+      }
+      if (lane == 31) {
+        cpre[n] = incl;
+        if (blockIdx.x == 0) d.cpre_g[n] = incl;
+      }
+    }
+  }
   __syncthreads();
 
   // =========================================================================
@@ -565,28 +625,61 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
     // Each stage's plan (and its block-table lookups, and a group's next
     // claim) is made one stage ahead, so those latencies overlap the previous
     // stage's empty-slot wait and copies.
-    auto claim = [&](int& item_, int& b_, int& h0_, int& pb_, int& pe_) -> bool {
+    // balanced split (transposed kernels): lane g's stream, next unit, end
+    const int* cpre = reinterpret_cast<const int*>(smem + d.cpre_off);
+    int bal_u = 0, bal_hi = 0, bal_rank = 0;
+    const int bal_sid0 = blockIdx.x * d.NG + lane;
+    if constexpr (TR) {
+      const int64_t T = cpre[d.nranks];
+      const int NS = (int)(T < d.nstreams ? T : (int64_t)d.nstreams);
+      if (lane < d.NG && bal_sid0 < NS) {
+        bal_u = (int)bal_bound(bal_sid0, T, NS);
+        bal_hi = (int)bal_bound(bal_sid0 + 1, T, NS);
+        int lo = 0, hi = d.nranks;                 // last rank with cpre <= bal_u
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (cpre[mid] <= bal_u) lo = mid; else hi = mid;
+        }
+        bal_rank = lo;
+      }
+    }
+    int g_real = 0;                                // pages of the current item that exist
+    auto claim = [&](int& item_, int& b_, int& h0_, int& pb_, int& pe_, int& real_) -> bool {
+      if constexpr (TR) {
+        if (bal_u >= bal_hi) return false;
+        while (cpre[bal_rank + 1] <= bal_u) ++bal_rank;   // ranks without units
+        const int c0 = cpre[bal_rank];
+        rank_units(d, bal_rank, real_);
+        item_ = bal_sid0 + bal_rank;
+        b_ = bal_rank / d.HGN;
+        h0_ = (bal_rank - b_ * d.HGN) * d.HG;
+        pb_ = bal_u - c0;
+        pe_ = min(bal_hi, cpre[bal_rank + 1]) - c0;
+        bal_u = c0 + pe_;
+        return true;
+      } else {
       for (;;) {
         const int item = (int)atomicAdd(d.counter, 1u);
         if (item >= d.n_items) return false;
         int b, z, s, pb, pe, nsplit;
         decode_item(d, item, b, z, s);
         if (!item_pages(d, b, s, pb, pe, nsplit)) continue;
-        item_ = item; b_ = b; h0_ = z * d.HG; pb_ = pb; pe_ = pe;
+        item_ = item; b_ = b; h0_ = z * d.HG; pb_ = pb; pe_ = pe; real_ = pe;
         return true;
+      }
       }
     };
     const int gl = min(lane / PPW, MAXG - 1), pp = lane % PPW;   // page slot l = gl*PPW + pp
     // block-table entry of this lane's page slot under a plan held by the group lanes
-    auto lookup = [&](bool act, int b_, int pg_, int pe_, bool& valid) -> int {
+    auto lookup = [&](bool act, int b_, int pg_, int pe_, int real_, bool& valid) -> int {
       const unsigned amask = __ballot_sync(0xffffffffu, act);
       const int s_b = __shfl_sync(0xffffffffu, b_, gl);
       const int s_pg = __shfl_sync(0xffffffffu, pg_, gl);
-      const int s_pe = __shfl_sync(0xffffffffu, pe_, gl);
+      const int s_pe = __shfl_sync(0xffffffffu, min(pe_, real_), gl);
       valid = lane < d.P && ((amask >> gl) & 1) && s_pg + pp < s_pe;
       return valid ? p.block_table[(int64_t)s_b * p.max_blocks + s_pg + pp] : -1;
     };
-    if (d.NG == 1) {
+    if (!TR && d.NG == 1) {
       constexpr int kCopies1 = 2 * PAGE;     // copy slots per page (12 used with adjacent rows, 32 without)
     // one group (HG = 8 heads per CTA): a single item stream, block-table
     // entries read one stage ahead.  Measured 18% faster than the general
@@ -672,23 +765,23 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
     int g_item = -1, g_b = 0, g_h0 = 0, g_pg = 0, g_pe = 0;
     bool g_active = false, g_exhausted = lane >= d.NG;
     if (!g_exhausted) {
-      g_active = claim(g_item, g_b, g_h0, g_pg, g_pe);
+      g_active = claim(g_item, g_b, g_h0, g_pg, g_pe, g_real);
       g_exhausted = !g_active;
     }
     bool pvalid;
-    int phys = lookup(g_active, g_b, g_pg, g_pe, pvalid);
+    int phys = lookup(g_active, g_b, g_pg, g_pe, g_real, pvalid);
     while (alive) {
       const unsigned active = __ballot_sync(0xffffffffu, g_active);
       if (active == 0) break;
       // plan of the next stage: the same item's next pages, or a new claim
-      int n_item = g_item, n_b = g_b, n_h0 = g_h0, n_pg = g_pg + PPW, n_pe = g_pe;
+      int n_item = g_item, n_b = g_b, n_h0 = g_h0, n_pg = g_pg + PPW, n_pe = g_pe, n_real = g_real;
       bool n_active = g_active && n_pg < n_pe;
       if (!n_active && !g_exhausted) {
-        n_active = claim(n_item, n_b, n_h0, n_pg, n_pe);
+        n_active = claim(n_item, n_b, n_h0, n_pg, n_pe, n_real);
         g_exhausted = !n_active;
       }
       bool n_pvalid;
-      const int n_phys = lookup(n_active, n_b, n_pg, n_pe, n_pvalid);
+      const int n_phys = lookup(n_active, n_b, n_pg, n_pe, n_real, n_pvalid);
       const int slot = it % NST;
       if (it >= NST && !mbar_wait(&empty_bar[slot], ((it / NST) - 1) & 1)) { alive = false; break; }
       const bool ok = pvalid && phys >= 0;
@@ -753,7 +846,7 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
         }
       }
       ++it;
-      g_item = n_item; g_b = n_b; g_h0 = n_h0; g_pg = n_pg; g_pe = n_pe; g_active = n_active;
+      g_item = n_item; g_b = n_b; g_h0 = n_h0; g_pg = n_pg; g_pe = n_pe; g_real = n_real; g_active = n_active;
       phys = n_phys;
       pvalid = n_pvalid;
     }
@@ -1233,9 +1326,26 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   const int h = blockIdx.x;
   const int nq = seq_nq(p, b);
   if (nq <= 0 || nq * d.G > d.max_rows) return;
-  const int kv_end = seq_kv_end(p, b, nq);
-  const int npg = (kv_end + dec::PAGE - 1) / dec::PAGE;
-  const int nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;   // partials (chunks) of this sequence
+  int nsplit, first;            // partials of this (sequence, head): first slot, count
+  int64_t pstride;              // rows between consecutive partials
+  if (d.tr) {
+    // balanced split: the streams holding units of this rank
+    const int rank = b * d.HGN + h / d.HG;
+    const int64_t T = d.cpre_g[d.nranks];
+    const int NS = (int)(T < d.nstreams ? T : (int64_t)d.nstreams);
+    const int u0 = d.cpre_g[rank], u1 = d.cpre_g[rank + 1];
+    if (u1 <= u0) return;
+    const int f = bal_sid(u0, T, NS), l = bal_sid(u1 - 1, T, NS);
+    nsplit = l - f + 1;
+    first = (f + rank) * d.HG + h % d.HG;
+    pstride = (int64_t)d.HG * d.R_pad;
+  } else {
+    const int kv_end = seq_kv_end(p, b, nq);
+    const int npg = (kv_end + dec::PAGE - 1) / dec::PAGE;
+    nsplit = npg == 0 ? 1 : (npg + d.CP - 1) / d.CP;   // partials (chunks) of this sequence
+    first = (b * p.num_heads_kv + h) * d.S_max;
+    pstride = d.R_pad;
+  }
   if (nsplit <= 1) return;
   const int R = nq * d.G;
   const int W = blockDim.x / (32 * d.max_rows);         // warps per row (uniform)
@@ -1246,10 +1356,10 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   // partial range of this warp: [s0, s1)
   const int per = (nsplit + W - 1) / W;
   const int s0 = min(nsplit, wi * per), s1 = min(nsplit, s0 + per);
-  const int64_t row0 = (((int64_t)b * p.num_heads_kv + h) * d.S_max) * d.R_pad + (active ? r : 0);
+  const int64_t row0 = (int64_t)first * d.R_pad + (active ? r : 0);
   float M = -INFINITY;
   if (active)
-    for (int s = s0 + lane; s < s1; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * d.R_pad].x);
+    for (int s = s0 + lane; s < s1; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * pstride].x);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float mu = M == -INFINITY ? 0.f : M;
@@ -1259,7 +1369,7 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   for (int base = s0; active && base < s1; base += 32) {
     float w = 0.f;
     if (base + lane < s1) {
-      const float2 ml = d.ml[row0 + (int64_t)(base + lane) * d.R_pad];
+      const float2 ml = d.ml[row0 + (int64_t)(base + lane) * pstride];
       w = ml.y * fast_exp2(ml.x - mu);
     }
     den += w;
@@ -1267,7 +1377,7 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
 #pragma unroll 4
     for (int j = 0; j < n; ++j) {
       const float wj = __shfl_sync(0xffffffffu, w, j);
-      const float4 v = *reinterpret_cast<const float4*>(op + (int64_t)(base + j) * d.R_pad * dec::D);
+      const float4 v = *reinterpret_cast<const float4*>(op + (int64_t)(base + j) * pstride * dec::D);
       num.x = fmaf(wj, v.x, num.x); num.y = fmaf(wj, v.y, num.y);
       num.z = fmaf(wj, v.z, num.z); num.w = fmaf(wj, v.w, num.w);
     }
@@ -1466,14 +1576,16 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // page-transposed V: the HG records back to back (ldmatrix rows are 16
   // consecutive bytes, conflict-free at any 16-byte aligned base)
   d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
-  d.tr = vq8t && R <= 8 && decode_tr_enabled() ? (d.HG == 1 ? NWC_TR : NWC) : 0;
+  d.nranks = p.num_seqs * d.HGN;
+  d.tr = vq8t && R <= 8 && d.nranks <= kMaxRanksTR && decode_tr_enabled() ? (d.HG == 1 ? NWC_TR : NWC) : 0;
   const int nwc = d.tr ? d.tr : NWC;
   d.P = nwc / d.HG;
   d.NG = nwc / d.HG;
   const int q_bytes = mt == 2 ? NWC * mt * 16 * QROW : 0;   // one Q tile per compute warp
+  const int cpre_bytes = d.tr ? ((d.nranks + 1) * 4 + 15) & ~15 : 0;
   constexpr int64_t kSmem = 227 * 1024;
   auto need = [&](int nst, int pages) {
-    return (int64_t)nst * pages * (d.kpage + d.vpage) + q_bytes;
+    return (int64_t)nst * pages * (d.kpage + d.vpage) + q_bytes + cpre_bytes;
   };
   // Two pages per warp and stage give each warp two independent streams of
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
@@ -1500,33 +1612,49 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     d.vbase = d.P * d.kpage;
   }
   d.q_off = d.nst * d.stage_bytes;
+  d.cpre_off = d.q_off;
   if (d.tr) d.tr_tab = choose_tr_table(d);
   d.scale_log2 = p.scale * kLog2e;
   // chunking: enough chunks to keep every SM busy several times over
   const int sms = num_sms();
+  d.nstreams = sms * d.NG;                 // transposed kernels: one CTA per SM
   const int max_pages = (p.max_kv + PAGE - 1) / PAGE;
   const int64_t est_pages = (int64_t)p.num_seqs * d.HGN * max_pages / 2 + 1;   // lengths ~ U[0, max]
   const int64_t want = est_pages / ((int64_t)sms * d.NG * 6);   // items per group stream
   int cp = (int)std::min<int64_t>(std::max<int64_t>(want, 16), 512);
   // at most kCombineMaxParts partials per (sequence, kv head)
   cp = std::max<int>(cp, (int)(((int64_t)max_pages + kCombineMaxParts - 1) / kCombineMaxParts));
-  cp = ((cp + d.P - 1) / d.P) * d.P;
+  if (const char* e = std::getenv("GFX906_FA_DECODE_CHUNK")) {   // tuning override: pages per chunk
+    const int v = std::atoi(e);
+    if (v > 0) cp = std::max<int>(v, (int)(((int64_t)max_pages + kCombineMaxParts - 1) / kCombineMaxParts));
+  }
+  cp = ((cp + d.ppw - 1) / d.ppw) * d.ppw;
   d.CP = cp;
   d.S_max = max_pages == 0 ? 1 : (max_pages + cp - 1) / cp;
   d.n_items = p.num_seqs * d.HGN * d.S_max;
   return cudaSuccess;
 }
 
+// Workspace: [0, 256) work-queue counter; rank prefix sums (transposed
+// kernels); partial O rows; (max, sum) per partial row.
+static size_t decode_ws_rows(const DecodeParams& d) {
+  if (d.tr) return ((size_t)d.nstreams + d.nranks) * d.HG * d.R_pad;   // slots s + rank
+  return (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+}
+static size_t decode_ws_cpre(const DecodeParams& d) {
+  return d.tr ? (((size_t)d.nranks + 1) * sizeof(int) + 255) & ~(size_t)255 : 0;
+}
 static size_t decode_ws_bytes(const DecodeParams& d) {
-  const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+  const size_t rows = decode_ws_rows(d);
   const size_t o = rows * dec::D * sizeof(float);
-  return 256 + ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
+  return 256 + decode_ws_cpre(d) + ((o + 255) & ~(size_t)255) + rows * sizeof(float2) + 256;
 }
 
 template <int MT, int VT, bool MASK>
 static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   // one Q tile per compute warp (MT == 2)
-  const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)dec::NWC * MT * 16 * dec::QROW : 0);
+  const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)dec::NWC * MT * 16 * dec::QROW : 0) +
+                      (d.tr ? (size_t)(d.nranks + 1) * sizeof(int) : 0);
   auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4, 1> : decode_kernel<MT, VT, MASK, 3, 1>;
   if constexpr (MT == 1) {
     if (d.ppw == 2) kern = decode_kernel<MT, VT, MASK, 3, 2>;
@@ -1541,11 +1669,11 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const int grid = std::max(1, std::min(d.n_items, num_sms()));
+  const int grid = d.tr ? d.nstreams / d.NG : std::max(1, std::min(d.n_items, num_sms()));
   kern<<<grid, d.tr == dec::NWC_TR ? dec::NTHREADS_TR : dec::NTHREADS, smem, stream>>>(d);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (d.S_max > 1) {
+  if (d.tr || d.S_max > 1) {   // balanced split: any rank may span streams
     const int cw = std::max(1, std::min(kCombineMaxW, 32 / d.max_rows));   // warps per row
     decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows * cw, 0, stream>>>(d);
     e = cudaGetLastError();
@@ -1578,11 +1706,12 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
   if (!workspace || workspace_bytes < decode_ws_bytes(d) || ((uintptr_t)workspace & 15)) return cudaErrorInvalidValue;
   {
     // [0, 256): work-queue counter; then partial O and (max, sum) rows
-    const size_t rows = (size_t)d.p.num_seqs * d.p.num_heads_kv * d.S_max * d.R_pad;
+    const size_t rows = decode_ws_rows(d), cp = decode_ws_cpre(d);
     uint8_t* w = reinterpret_cast<uint8_t*>(workspace);
     d.counter = reinterpret_cast<unsigned int*>(w);
-    d.opart = reinterpret_cast<float*>(w + 256);
-    d.ml = reinterpret_cast<float2*>(w + 256 + (((rows * dec::D * sizeof(float)) + 255) & ~(size_t)255));
+    d.cpre_g = reinterpret_cast<int*>(w + 256);
+    d.opart = reinterpret_cast<float*>(w + 256 + cp);
+    d.ml = reinterpret_cast<float2*>(w + 256 + cp + (((rows * dec::D * sizeof(float)) + 255) & ~(size_t)255));
     cudaError_t ze = cudaMemsetAsync(d.counter, 0, sizeof(unsigned int), stream);
     if (ze != cudaSuccess) return ze;
   }
