@@ -93,6 +93,7 @@ struct DecodeParams {
   int q_off;              // smem offset of the Q tiles (MT == 2)
   int max_rows;           // sequences with n_q * G above this are left to the prefill kernel
   int nst;                // pipeline slots of this launch
+  int nt;                 // transposed consumer: n-tiles of 8 query rows
   int tr;                 // 0, or compute warps of the transposed consumer (<= 8 rows, page-transposed Q8_0 V)
   // Balanced split (the transposed kernels): units = pages of each rank
   // (sequence b, head group z; rank = b*HGN + z) in rank order; stream s of
@@ -100,6 +101,7 @@ struct DecodeParams {
   // N = min(nstreams, T).  A stream's piece of one rank is a segment; its
   // partial result goes to slot s + rank.
   int nranks, nstreams;
+  int qtr_off;            // smem offset of the transposed consumer's Q tiles (three n-tiles)
   int cpre_off;           // smem offset of the rank prefix sums (nranks + 1 ints)
   int* cpre_g;            // the same prefix sums, written by CTA 0 for the combine
   uint32_t tr_tab;        // transposed consumer: key order per quad (see decode_consumer_tr)
@@ -215,7 +217,7 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 
 constexpr float kRescaleLog2T = 6.0f;     // P <= 2^6: P * s_v stays finite in fp16 for any fp16 V
 
-template <bool MASK, int NST, int PPW, int NW>
+template <bool MASK, int NST, int PPW, int NW, int NT>
 __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_t* smem, uint64_t* full_bar,
                                                    uint64_t* empty_bar, StageMeta* meta, int warp, int lane) {
   using namespace dec;
@@ -239,79 +241,115 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
   const uint32_t kofA = (uint32_t)((tA >> 2) * d.kgs + (tA & 3) * hgb_k + hl * d.rb_k);
   const uint32_t kofB = (uint32_t)((tB >> 2) * d.kgs + (tB & 3) * hgb_k + hl * d.rb_k);
 
-  float o[8][4];           // O^T: m-tile mt = dims 16mt .. 16mt+15; columns = rows 2*j4, 2*j4+1
-  float corr[4];           // row `blk` of this tile: sum over keys of (P s_v) for block blk
-  uint32_t qb[8][2];       // Q^T B fragments per 16-dim k-step
-  float kc[4][2];          // -1152 * sum of block blk's Q dims, rows 2*j4, 2*j4+1
-  float mrow[2], lrow[2];
-  // item state kept live: rows, and per row of this thread (2*j4 + c) the
-  // exclusive end of its visible keys (-1 for a padding row); the rest is
-  // decoded from the item again at the epilogue
+  // n-tile nt holds query rows 8*nt .. 8*nt+7; this thread's accumulator
+  // columns are rows 8*nt + 2*j4 + c, c = 0, 1
+  // With three n-tiles the Q^T fragments live in this warp's shared-memory
+  // Q tile (fp16 rows, QROW bytes apart) and are loaded per block with
+  // ldmatrix; with fewer they stay in registers.
+  constexpr bool QSM = NT >= 3;
+  float o[NT][8][4];       // O^T: m-tile mt = dims 16mt .. 16mt+15
+  float corr[NT][4];       // row `blk` of this tile: sum over keys of (P s_v) for block blk
+  uint32_t qb[QSM ? 1 : NT][8][2];   // Q^T B fragments per 16-dim k-step (registers)
+  float kc[QSM ? 1 : NT][4][2];   // -1152 * sum of block blk's Q dims, per column row (registers)
+  float mrow[NT][2], lrow[NT][2];
+  // item state kept live: rows, and per column row the exclusive end of its
+  // visible keys (-1 for a padding row); the rest is decoded from the item
+  // again at the epilogue
   int cur_item = -1, cR = 0;
-  int klim[2] = {-1, -1};
+  int klim[NT][2];
 
   const uint32_t smem_base = smem_u32(smem);
   auto ld16 = [&](uint32_t a) { return (uint32_t)*reinterpret_cast<const uint16_t*>(smem + (a - smem_base)); };
   auto ld64 = [&](uint32_t a) { return *reinterpret_cast<const uint2*>(smem + (a - smem_base)); };
+  // per warp: the Q tile, then the K-offset constants [nt][blk][row] (fp32)
+  const uint32_t qs_base = smem_base + d.qtr_off + warp * (NT * 8 * QROW + 512);
+  const uint32_t qk_base = qs_base + NT * 8 * QROW;
+  // B fragments of k-steps 2*blk and 2*blk + 1 for n-tile nt: {b0, b1} each
+  auto q_frags = [&](int nt, int blk, uint32_t q4[4]) {
+    if constexpr (QSM) {
+      const int mi = lane >> 3, ri = lane & 7;
+      ldmatrix_x4(q4, qs_base + (8 * nt + ri) * QROW + ((2 * blk + (mi >> 1)) * 16 + (mi & 1) * 8) * 2);
+    } else {
+      q4[0] = qb[nt][2 * blk][0]; q4[1] = qb[nt][2 * blk][1];
+      q4[2] = qb[nt][2 * blk + 1][0]; q4[3] = qb[nt][2 * blk + 1][1];
+    }
+  };
 
   auto start_item = [&](int b, int h) {
+    if constexpr (QSM) __syncwarp();
 #pragma unroll
-    for (int mt = 0; mt < 8; ++mt)
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) o[mt][c] = 0.f;
+      for (int mt = 0; mt < 8; ++mt)
 #pragma unroll
-    for (int c = 0; c < 4; ++c) corr[c] = 0.f;
-    mrow[0] = mrow[1] = -INFINITY;
-    lrow[0] = lrow[1] = 0.f;
-    // Q row rq: dims 16ks + 2*j4 (+1) and 16ks + 2*j4 + 8 (+9); all loads first
-    const bool v = rq < cR;
-    const int t = v ? rq / d.G : 0;
-    const int64_t base = v ? q_offset(p, b, t, h * d.G + (rq - t * d.G)) : 0;
-    float qf[16][2];
-    if (p.q_dtype == DT_F32) {
-      const float* q = reinterpret_cast<const float*>(p.q);
-      float2 x[16];
+        for (int c = 0; c < 4; ++c) o[nt][mt][c] = 0.f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        x[i] = v ? *reinterpret_cast<const float2*>(q + base + (i >> 1) * 16 + (i & 1) * 8 + 2 * j4)
-                 : make_float2(0.f, 0.f);
+      for (int c = 0; c < 4; ++c) corr[nt][c] = 0.f;
+      mrow[nt][0] = mrow[nt][1] = -INFINITY;
+      lrow[nt][0] = lrow[nt][1] = 0.f;
+    }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) { qf[i][0] = x[i].x; qf[i][1] = x[i].y; }
-    } else {
-      const uint16_t* q = reinterpret_cast<const uint16_t*>(p.q);
-      uint32_t x[16];
+    for (int nt = 0; nt < NT; ++nt) {
+      // Q row 8nt + rq: dims 16ks + 2*j4 (+1) and 16ks + 2*j4 + 8 (+9); all loads first
+      const int rr = 8 * nt + rq;
+      const bool v = rr < cR;
+      const int t = v ? rr / d.G : 0;
+      const int64_t base = v ? q_offset(p, b, t, h * d.G + (rr - t * d.G)) : 0;
+      float qf[16][2];
+      if (p.q_dtype == DT_F32) {
+        const float* q = reinterpret_cast<const float*>(p.q);
+        float2 x[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        x[i] = v ? *reinterpret_cast<const uint32_t*>(q + base + (i >> 1) * 16 + (i & 1) * 8 + 2 * j4) : 0u;
-      const bool bf = p.q_dtype == DT_BF16;
+        for (int i = 0; i < 16; ++i)
+          x[i] = v ? *reinterpret_cast<const float2*>(q + base + (i >> 1) * 16 + (i & 1) * 8 + 2 * j4)
+                   : make_float2(0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) { qf[i][0] = x[i].x; qf[i][1] = x[i].y; }
+      } else {
+        const uint16_t* q = reinterpret_cast<const uint16_t*>(p.q);
+        uint32_t x[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          x[i] = v ? *reinterpret_cast<const uint32_t*>(q + base + (i >> 1) * 16 + (i & 1) * 8 + 2 * j4) : 0u;
+        const bool bf = p.q_dtype == DT_BF16;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if (bf) {
+            qf[i][0] = __uint_as_float(x[i] << 16);
+            qf[i][1] = __uint_as_float(x[i] & 0xffff0000u);
+          } else {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x[i]));
+            qf[i][0] = f.x;
+            qf[i][1] = f.y;
+          }
+        }
+      }
+      float qs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        if (bf) {
-          qf[i][0] = __uint_as_float(x[i] << 16);
-          qf[i][1] = __uint_as_float(x[i] & 0xffff0000u);
+        const uint32_t hq = pack_half2(qf[i][0], qf[i][1]);
+        if constexpr (QSM)
+          asm volatile("st.shared.u32 [%0], %1;" ::"r"(qs_base + rr * QROW + ((i >> 1) * 16 + (i & 1) * 8 + 2 * j4) * 2),
+                       "r"(hq));
+        else
+          qb[nt][i >> 1][i & 1] = hq;
+        const float2 r = __half22float2(*reinterpret_cast<const __half2*>(&hq));   // the values the MMA sees
+        qs[i >> 2] += r.x + r.y;
+      }
+#pragma unroll
+      for (int blk = 0; blk < 4; ++blk) {
+        float s = qs[blk];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);       // row rr's block sum, on all 4 lanes of the quad
+        if constexpr (QSM) {
+          if (j4 == 0) asm volatile("st.shared.f32 [%0], %1;" ::"r"(qk_base + ((nt * 4 + blk) * 8 + rq) * 4), "f"(-1152.f * s));
         } else {
-          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&x[i]));
-          qf[i][0] = f.x;
-          qf[i][1] = f.y;
+          kc[nt][blk][0] = -1152.f * __shfl_sync(0xffffffffu, s, 8 * j4);
+          kc[nt][blk][1] = -1152.f * __shfl_sync(0xffffffffu, s, 8 * j4 + 4);
         }
       }
     }
-    float qs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t hq = pack_half2(qf[i][0], qf[i][1]);
-      qb[i >> 1][i & 1] = hq;
-      const float2 r = __half22float2(*reinterpret_cast<const __half2*>(&hq));   // the values the MMA sees
-      qs[i >> 2] += r.x + r.y;
-    }
-#pragma unroll
-    for (int blk = 0; blk < 4; ++blk) {
-      float s = qs[blk];
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);       // row rq's block sum, on all 4 lanes of the quad
-      kc[blk][0] = -1152.f * __shfl_sync(0xffffffffu, s, 8 * j4);
-      kc[blk][1] = -1152.f * __shfl_sync(0xffffffffu, s, 8 * j4 + 4);
-    }
+    if constexpr (QSM) __syncwarp();
   };
 
   // balanced split: this warp's stream and the rank prefix sums
@@ -325,49 +363,53 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
     const int cb = rank / d.HGN, cz = rank - cb * d.HGN;
     // the stream holds the whole rank: final output, else a partial
     const bool whole = cpre[rank] >= bal_bound(sid, T, NS) && cpre[rank + 1] <= bal_bound(sid + 1, T, NS);
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      float v = lrow[c];
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      v += __shfl_xor_sync(0xffffffffu, v, 8);
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      lrow[c] = v;
-    }
-    float cv[4][2];
-#pragma unroll
-    for (int blk = 0; blk < 4; ++blk) {
-      cv[blk][0] = 1152.f * __shfl_sync(0xffffffffu, corr[0], 4 * blk + j4);
-      cv[blk][1] = 1152.f * __shfl_sync(0xffffffffu, corr[1], 4 * blk + j4);
-    }
     const int h = cz * d.HG + hl;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int r = 2 * j4 + c;
-      if (r >= cR) continue;
-      const float l = lrow[c];
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      if (whole) {
-        const int t = r / d.G;
-        const int hq = h * d.G + (r - t * d.G);
-        const int64_t ob = o_offset(p, cb, t, hq);
+    for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
+      for (int c = 0; c < 2; ++c) {
+        float v = lrow[nt][c];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        lrow[nt][c] = v;
+      }
+      float cv[4][2];
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const float x = (o[mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
-            const int64_t off = ob + mt * 16 + hh * 8 + rq;
-            if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = x;
-            else if (p.out_dtype == DT_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
-            else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
-          }
-      } else {
-        const int64_t row = ((int64_t)cur_item * d.HG + hl) * d.R_pad + r;
-        float* op = d.opart + row * D;
+      for (int blk = 0; blk < 4; ++blk) {
+        cv[blk][0] = 1152.f * __shfl_sync(0xffffffffu, corr[nt][0], 4 * blk + j4);
+        cv[blk][1] = 1152.f * __shfl_sync(0xffffffffu, corr[nt][1], 4 * blk + j4);
+      }
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt)
+      for (int c = 0; c < 2; ++c) {
+        const int r = 8 * nt + 2 * j4 + c;
+        if (r >= cR) continue;
+        const float l = lrow[nt][c];
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        if (whole) {
+          const int t = r / d.G;
+          const int hq = h * d.G + (r - t * d.G);
+          const int64_t ob = o_offset(p, cb, t, hq);
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) op[mt * 16 + hh * 8 + rq] = (o[mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
-        if (rq == 0) d.ml[row] = make_float2(mrow[c], l);
+          for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const float x = (o[nt][mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
+              const int64_t off = ob + mt * 16 + hh * 8 + rq;
+              if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = x;
+              else if (p.out_dtype == DT_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
+              else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
+            }
+        } else {
+          const int64_t row = ((int64_t)cur_item * d.HG + hl) * d.R_pad + r;
+          float* op = d.opart + row * D;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh)
+              op[mt * 16 + hh * 8 + rq] = (o[nt][mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
+          if (rq == 0) d.ml[row] = make_float2(mrow[nt][c], l);
+        }
       }
     }
   };
@@ -388,12 +430,14 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
       const int ckv = p.kv_len[cb];
       const int cqabs = p.q_abs ? p.q_abs[cb] : 0;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int r = 2 * j4 + c;
-        int lim = ckv;
-        if (p.q_abs) lim = min(lim, cqabs + r / d.G + 1);
-        klim[c] = r < cR ? lim : -1;
-      }
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int r = 8 * nt + 2 * j4 + c;
+          int lim = ckv;
+          if (p.q_abs) lim = min(lim, cqabs + r / d.G + 1);
+          klim[nt][c] = r < cR ? lim : -1;
+        }
       start_item(cb, cz * d.HG + hl);
     }
     bool pok[PPW];
@@ -408,14 +452,16 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
 #pragma unroll
       for (int pp = 0; pp < PPW; ++pp) psrc[pp] = sub * PPW + (pok[pp] ? pp : first_ok);
       const uint32_t stage_base = smem_base + slot * d.stage_bytes;
-      // ---------------- S^T = K Q^T ------------------------------------------
-      float sacc[PPW][4];
+      // ---------------- S^T = K Q^T (K fragments shared by the n-tiles) --------
+      float sacc[PPW][NT][4];
 #pragma unroll
       for (int pp = 0; pp < PPW; ++pp) {
         const uint32_t kb = stage_base + psrc[pp] * d.kps;
         const uint32_t rA = kb + kofA, rB = kb + kofB;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) sacc[pp][c] = 0.f;
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) sacc[pp][nt][c] = 0.f;
 #pragma unroll
         for (int blk = 0; blk < 4; ++blk) {
           const uint32_t cA = rA + blk * QBLOCK + 2 + 2 * j4, cB = rB + blk * QBLOCK + 2 + 2 * j4;
@@ -430,89 +476,111 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
           a1[3] = i8x2_to_h2_biased(ld16(cB + 24));
           const float dA = half_bits_to_float((uint16_t)ld16(rA + blk * QBLOCK));
           const float dB = half_bits_to_float((uint16_t)ld16(rB + blk * QBLOCK));
-          float acc[4];
-          mma_f16_16816_c(acc, a0, qb[2 * blk], kc[blk][0], kc[blk][1]);
-          mma_f16_16816(acc, a1, qb[2 * blk + 1]);
-          sacc[pp][0] = fmaf(acc[0], dA, sacc[pp][0]);
-          sacc[pp][1] = fmaf(acc[1], dA, sacc[pp][1]);
-          sacc[pp][2] = fmaf(acc[2], dB, sacc[pp][2]);
-          sacc[pp][3] = fmaf(acc[3], dB, sacc[pp][3]);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t q4[4];
+            q_frags(nt, blk, q4);
+            float acc[4];
+            float k0, k1;
+            if constexpr (QSM) {
+              const float2 kk = *reinterpret_cast<const float2*>(smem + (qk_base - smem_base) + ((nt * 4 + blk) * 8 + 2 * j4) * 4);
+              k0 = kk.x; k1 = kk.y;
+            } else {
+              k0 = kc[nt][blk][0]; k1 = kc[nt][blk][1];
+            }
+            mma_f16_16816_c(acc, a0, q4, k0, k1);
+            mma_f16_16816(acc, a1, q4 + 2);
+            sacc[pp][nt][0] = fmaf(acc[0], dA, sacc[pp][nt][0]);
+            sacc[pp][nt][1] = fmaf(acc[1], dA, sacc[pp][nt][1]);
+            sacc[pp][nt][2] = fmaf(acc[2], dB, sacc[pp][nt][2]);
+            sacc[pp][nt][3] = fmaf(acc[3], dB, sacc[pp][nt][3]);
+          }
         }
       }
       // ---------------- mask + online softmax (base 2, lazy max) --------------
-      float tmx[2] = {-INFINITY, -INFINITY};
+      float tmx[NT][2];
+      bool grow = false;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int kv_lim = klim[c];
-#pragma unroll
-        for (int pp = 0; pp < PPW; ++pp) {
-          const int k0 = (page0 + pp) * PAGE;
-          const bool page_full = !MASK && pok[pp] && k0 + PAGE <= kv_lim;
-#pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            float x = sacc[pp][2 * hb + c] * d.scale_log2;
-            if (!page_full) {
-              const int k = k0 + (hb ? tB : tA);
-              if constexpr (MASK) {
-                if (pok[pp] && k < kv_lim) {
-                  const int cb = (cur_item - sid) / d.HGN;
-                  const int t = (2 * j4 + c) / d.G;
-                  x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
-                      (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
-                }
-              }
-              x = (pok[pp] && k < kv_lim) ? x : -INFINITY;
-            }
-            sacc[pp][2 * hb + c] = x;
-            tmx[c] = fmaxf(tmx[c], x);
-          }
-        }
-      }
-      const bool grow = tmx[0] > mrow[0] + kRescaleLog2T || tmx[1] > mrow[1] + kRescaleLog2T;
-      if (__any_sync(0xffffffffu, grow)) {
-        float alpha[2];
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          float mx = tmx[c];
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-          alpha[c] = 1.f;
-          if (mx > mrow[c] + kRescaleLog2T) {        // uniform over the lanes of this row
-            alpha[c] = fast_exp2(mrow[c] - mx);
-            mrow[c] = mx;
-            lrow[c] *= alpha[c];
+          const int kv_lim = klim[nt][c];
+          tmx[nt][c] = -INFINITY;
+#pragma unroll
+          for (int pp = 0; pp < PPW; ++pp) {
+            const int k0 = (page0 + pp) * PAGE;
+            const bool page_full = !MASK && pok[pp] && k0 + PAGE <= kv_lim;
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb) {
+              float x = sacc[pp][nt][2 * hb + c] * d.scale_log2;
+              if (!page_full) {
+                const int k = k0 + (hb ? tB : tA);
+                if constexpr (MASK) {
+                  if (pok[pp] && k < kv_lim) {
+                    const int cb = (cur_item - sid) / d.HGN;
+                    const int t = (8 * nt + 2 * j4 + c) / d.G;
+                    x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
+                        (int64_t)cb * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+                  }
+                }
+                x = (pok[pp] && k < kv_lim) ? x : -INFINITY;
+              }
+              sacc[pp][nt][2 * hb + c] = x;
+              tmx[nt][c] = fmaxf(tmx[nt][c], x);
+            }
           }
+          grow |= tmx[nt][c] > mrow[nt][c] + kRescaleLog2T;
+        }
+      if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          float alpha[2];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float mx = tmx[nt][c];
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            alpha[c] = 1.f;
+            if (mx > mrow[nt][c] + kRescaleLog2T) {        // uniform over the lanes of this row
+              alpha[c] = fast_exp2(mrow[nt][c] - mx);
+              mrow[nt][c] = mx;
+              lrow[nt][c] *= alpha[c];
+            }
+          }
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            o[nt][mt][0] *= alpha[0]; o[nt][mt][2] *= alpha[0];
+            o[nt][mt][1] *= alpha[1]; o[nt][mt][3] *= alpha[1];
+          }
+          corr[nt][0] *= alpha[0]; corr[nt][2] *= alpha[0];
+          corr[nt][1] *= alpha[1]; corr[nt][3] *= alpha[1];
+        }
+      }
+      uint32_t pb[PPW][NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const float mu = mrow[nt][c] == -INFINITY ? 0.f : mrow[nt][c];
+          float ls = 0.f;
+#pragma unroll
+          for (int pp = 0; pp < PPW; ++pp)
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb) {
+              const float pv = fast_exp2(sacc[pp][nt][2 * hb + c] - mu);
+              sacc[pp][nt][2 * hb + c] = pv;
+              ls += pv;
+            }
+          lrow[nt][c] += ls;
         }
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          o[mt][0] *= alpha[0]; o[mt][2] *= alpha[0];
-          o[mt][1] *= alpha[1]; o[mt][3] *= alpha[1];
+        for (int pp = 0; pp < PPW; ++pp) {
+          pb[pp][nt][0] = movmatrix_trans(pack_half2(sacc[pp][nt][0], sacc[pp][nt][1]));
+          pb[pp][nt][1] = movmatrix_trans(pack_half2(sacc[pp][nt][2], sacc[pp][nt][3]));
         }
-        corr[0] *= alpha[0]; corr[2] *= alpha[0];
-        corr[1] *= alpha[1]; corr[3] *= alpha[1];
       }
-      uint32_t pb[PPW][2];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const float mu = mrow[c] == -INFINITY ? 0.f : mrow[c];
-        float ls = 0.f;
-#pragma unroll
-        for (int pp = 0; pp < PPW; ++pp)
-#pragma unroll
-          for (int hb = 0; hb < 2; ++hb) {
-            const float pv = fast_exp2(sacc[pp][2 * hb + c] - mu);
-            sacc[pp][2 * hb + c] = pv;
-            ls += pv;
-          }
-        lrow[c] += ls;
-      }
-#pragma unroll
-      for (int pp = 0; pp < PPW; ++pp) {
-        pb[pp][0] = movmatrix_trans(pack_half2(sacc[pp][0], sacc[pp][1]));
-        pb[pp][1] = movmatrix_trans(pack_half2(sacc[pp][2], sacc[pp][3]));
-      }
-      // ---------------- O^T += V^T P^T ------------------------------------------
+      // ---------------- O^T += V^T P^T (V fragments shared by the n-tiles) -----
       const uint32_t ones = 0x3c003c00u;
 #pragma unroll
       for (int pp = 0; pp < PPW; ++pp) {
@@ -522,8 +590,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
           uint32_t r4[4];
           ldmatrix_x4(r4, vrec + 2 * 4 * PAGE + (blk * 32 + lane) * PAGE);
           const uint2 sc = ld64(vrec + blk * 2 * PAGE + 8 * j4);
-          const uint32_t bq[2] = {hmul2_u32(pb[pp][0], __byte_perm(sc.x, sc.y, ssel_lo)),
-                                  hmul2_u32(pb[pp][1], __byte_perm(sc.x, sc.y, ssel_hi))};
+          const uint32_t s_lo = __byte_perm(sc.x, sc.y, ssel_lo), s_hi = __byte_perm(sc.x, sc.y, ssel_hi);
           uint32_t w[4];
 #pragma unroll
           for (int m = 0; m < 4; ++m) w[m] = r4[m] ^ 0x80808080u;
@@ -531,11 +598,15 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
                                    __byte_perm(w[0], 0x64646464u, sel_hi), __byte_perm(w[1], 0x64646464u, sel_hi)};
           const uint32_t av1[4] = {__byte_perm(w[2], 0x64646464u, sel_lo), __byte_perm(w[3], 0x64646464u, sel_lo),
                                    __byte_perm(w[2], 0x64646464u, sel_hi), __byte_perm(w[3], 0x64646464u, sel_hi)};
-          mma_f16_16816(o[2 * blk], av0, bq);
-          mma_f16_16816(o[2 * blk + 1], av1, bq);
           const uint32_t a1s = rq == blk ? ones : 0u;
           const uint32_t aones[4] = {a1s, 0u, a1s, 0u};
-          mma_f16_16816(corr, aones, bq);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint32_t bq[2] = {hmul2_u32(pb[pp][nt][0], s_lo), hmul2_u32(pb[pp][nt][1], s_hi)};
+            mma_f16_16816(o[nt][2 * blk], av0, bq);
+            mma_f16_16816(o[nt][2 * blk + 1], av1, bq);
+            mma_f16_16816(corr[nt], aones, bq);
+          }
         }
       }
     }
@@ -548,9 +619,9 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
 // MT: 16-row m-tiles (1 or 2).  VT: V format (0 fp16, 1 bf16, 2 Q8_0 rows,
 // 3 Q8_0 page-transposed records).
 // NST: shared-memory pipeline slots.  PPW: pages per compute warp per stage.
-// TRW: 0, or the compute warps (8 or 16) of the transposed consumer (MT 1,
-// VT 3 only).
-template <int MT, int VT, bool MASK, int NST, int PPW, int TRW = 0>
+// TRW: 0, or the compute warps (8 or 16) of the transposed consumer (MT 1 or
+// 2, VT 3 only) with NT n-tiles of 8 query rows.
+template <int MT, int VT, bool MASK, int NST, int PPW, int TRW = 0, int NT = 1>
 __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::NTHREADS, 1)
     decode_kernel(const DecodeParams d) {
   constexpr bool TR = TRW != 0;
@@ -868,8 +939,8 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
   // compute warps
   // =========================================================================
   if constexpr (TR) {
-    static_assert(MT == 1 && VT == 3, "transposed consumer: one m-tile, page-transposed Q8_0 V");
-    decode_consumer_tr<MASK, NST, PPW, NWC>(d, smem, full_bar, empty_bar, meta, warp, lane);
+    static_assert(VT == 3, "transposed consumer: page-transposed Q8_0 V");
+    decode_consumer_tr<MASK, NST, PPW, NWC, NT>(d, smem, full_bar, empty_bar, meta, warp, lane);
   } else {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
   const int hl = warp % d.HG;       // local kv head
@@ -1503,6 +1574,18 @@ static bool decode_tr_enabled() {
   return on;
 }
 
+// Most query rows per kv head (n_q * G) a sequence may have to be handled by
+// the decode kernel; longer ones go to the prefill kernel.  24 when the
+// transposed consumer (up to three 8-row n-tiles) serves the batch, else 32
+// (two 16-row m-tiles).  The dispatcher and plan_decode both use it.
+int decode_row_cap(const G9AttnBatch& p) {
+  const int G = p.num_heads_kv > 0 ? p.num_heads_q / p.num_heads_kv : 0;
+  const int HG = p.num_heads_kv % 8 == 0 ? 8 : (p.num_heads_kv % 4 == 0 ? 4 : (p.num_heads_kv % 2 == 0 ? 2 : 1));
+  const bool tr = p.v_fmt == G9_VFMT_Q8T && G >= 1 && G <= 24 && p.num_heads_kv > 0 &&
+                  (int64_t)p.num_seqs * (p.num_heads_kv / HG) <= dec::kMaxRanksTR && decode_tr_enabled();
+  return tr ? 24 : 32;
+}
+
 // Fills DecodeParams from the batch; returns cudaErrorInvalidValue when the
 // batch is outside what the decode kernel handles.
 static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
@@ -1518,7 +1601,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   d = DecodeParams{};
   d.p = p;
   d.G = p.num_heads_q / p.num_heads_kv;
-  const int R = std::min(d.G * std::max(p.seq_q, 1), 32);
+  const int R = std::min(d.G * std::max(p.seq_q, 1), decode_row_cap(p));
   mt = R <= 16 ? 1 : 2;
   d.max_rows = R;
   d.R_pad = 16 * mt;
@@ -1577,12 +1660,16 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // consecutive bytes, conflict-free at any 16-byte aligned base)
   d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
   d.nranks = p.num_seqs * d.HGN;
-  d.tr = vq8t && R <= 8 && d.nranks <= kMaxRanksTR && decode_tr_enabled() ? (d.HG == 1 ? NWC_TR : NWC) : 0;
+  // transposed consumer: up to 3 n-tiles of 8 query rows; 16 compute warps
+  // only for one n-tile and one kv head per CTA (register budget)
+  d.nt = (R + 7) / 8;
+  d.tr = vq8t && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled()
+             ? (d.HG == 1 && d.nt == 1 ? NWC_TR : NWC) : 0;
   const int nwc = d.tr ? d.tr : NWC;
   d.P = nwc / d.HG;
   d.NG = nwc / d.HG;
-  const int q_bytes = mt == 2 ? NWC * mt * 16 * QROW : 0;   // one Q tile per compute warp
-  const int cpre_bytes = d.tr ? ((d.nranks + 1) * 4 + 15) & ~15 : 0;
+  const int q_bytes = mt == 2 && !d.tr ? NWC * mt * 16 * QROW : 0;   // one Q tile per compute warp
+  const int cpre_bytes = (d.tr ? ((d.nranks + 1) * 4 + 15) & ~15 : 0) + (d.tr && d.nt >= 3 ? NWC * (24 * QROW + 512) : 0);
   constexpr int64_t kSmem = 227 * 1024;
   auto need = [&](int nst, int pages) {
     return (int64_t)nst * pages * (d.kpage + d.vpage) + q_bytes + cpre_bytes;
@@ -1591,7 +1678,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
   // (one m-tile only: with two the registers would spill); else one page per
   // warp with 4 stages, or 3 when 4 do not fit.
-  if (d.tr != NWC_TR && mt == 1 && 2 * d.P <= 8 && need(3, 2 * d.P) <= kSmem) {
+  if (d.tr != NWC_TR && (d.tr ? d.nt == 1 : mt == 1) && 2 * d.P <= 8 && need(3, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = 3;
@@ -1613,6 +1700,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   }
   d.q_off = d.nst * d.stage_bytes;
   d.cpre_off = d.q_off;
+  d.qtr_off = d.q_off + (((d.nranks + 1) * 4 + 15) & ~15);
   if (d.tr) d.tr_tab = choose_tr_table(d);
   d.scale_log2 = p.scale * kLog2e;
   // chunking: enough chunks to keep every SM busy several times over
@@ -1653,18 +1741,28 @@ static size_t decode_ws_bytes(const DecodeParams& d) {
 template <int MT, int VT, bool MASK>
 static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   // one Q tile per compute warp (MT == 2)
-  const size_t smem = (size_t)d.q_off + (MT == 2 ? (size_t)dec::NWC * MT * 16 * dec::QROW : 0) +
-                      (d.tr ? (size_t)(d.nranks + 1) * sizeof(int) : 0);
+  const size_t smem = (size_t)d.q_off + (MT == 2 && !d.tr ? (size_t)dec::NWC * MT * 16 * dec::QROW : 0) +
+                      (d.tr ? (size_t)((((d.nranks + 1) * 4 + 15) & ~15) + (d.nt >= 3 ? dec::NWC * (24 * dec::QROW + 512) : 0))
+                            : 0);
   auto kern = d.nst == 4 ? decode_kernel<MT, VT, MASK, 4, 1> : decode_kernel<MT, VT, MASK, 3, 1>;
   if constexpr (MT == 1) {
     if (d.ppw == 2) kern = decode_kernel<MT, VT, MASK, 3, 2>;
     if constexpr (VT == 3) {
       if (d.tr == dec::NWC_TR) {
         kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC_TR> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC_TR>;
-      } else if (d.tr) {
+      } else if (d.tr && d.nt == 1) {
         kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC>;
         if (d.ppw == 2) kern = decode_kernel<1, 3, MASK, 3, 2, dec::NWC>;
+      } else if (d.tr) {
+        kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC, 2> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC, 2>;
       }
+    }
+  } else if constexpr (VT == 3) {
+    if (d.tr) {
+      if (d.nt == 3)
+        kern = d.nst == 4 ? decode_kernel<2, 3, MASK, 4, 1, dec::NWC, 3> : decode_kernel<2, 3, MASK, 3, 1, dec::NWC, 3>;
+      else
+        kern = d.nst == 4 ? decode_kernel<2, 3, MASK, 4, 1, dec::NWC, 2> : decode_kernel<2, 3, MASK, 3, 1, dec::NWC, 2>;
     }
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -3,8 +3,9 @@
 // attention launchers on top of that.
 //
 // Routing rule, evaluated per sequence on the device by both kernels: a
-// sequence whose GQA-packed query rows (n_q * Hq/Hkv) fit in 32 goes to the
-// decode kernel, which streams its Q8 pages once; longer query chunks go to
+// sequence whose GQA-packed query rows (n_q * Hq/Hkv) fit in the decode row
+// cap (decode_row_cap: 24 for the transposed decode consumer, else 32) goes to
+// the decode kernel, which streams its Q8 pages once; longer query chunks go to
 // the tensor-core prefill kernel.  Host-side n_q / kv_len bounds, when the
 // caller has them (vLLM's metadata builder does), size the prefill workspace
 // exactly; otherwise seq_q / max_kv bound every sequence.
@@ -17,13 +18,12 @@ namespace g9 {
 cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, const int* nq_cap,
                         const int* kv_cap, int min_rows, void* ws, size_t ws_bytes, cudaStream_t stream);
 size_t prefill_ws_bytes(const G9AttnBatch& p, int nseq, const int* nq_cap, const int* kv_cap);
+int decode_row_cap(const G9AttnBatch& p);
 }  // namespace g9
 
 using namespace g9;
 
 namespace {
-
-constexpr int kDecodeRows = 32;
 
 struct Route {
   bool decode = false;
@@ -35,12 +35,13 @@ struct Route {
 Route route(const G9AttnBatch& b, const int* nq_host, const int* kv_host, bool allow_decode) {
   Route r;
   const int G = b.num_heads_q / std::max(1, b.num_heads_kv);
+  const int cap = decode_row_cap(b);
   for (int i = 0; i < b.num_seqs; ++i) {
     const int nq = nq_host ? nq_host[i] : b.seq_q;
     const int kv = kv_host ? kv_host[i] : b.max_kv;
     if (nq <= 0) continue;
     // nq is exact with host n_q, an upper bound (seq_q) without
-    const bool surely_small = (int64_t)nq * G <= kDecodeRows;
+    const bool surely_small = (int64_t)nq * G <= cap;
     const bool maybe_small = nq_host ? surely_small : true;
     if (allow_decode && maybe_small) r.decode = true;
     if (allow_decode && surely_small) continue;
@@ -74,7 +75,7 @@ cudaError_t attention_impl(const G9AttnBatch& b, const int* nq_host, const int* 
   uint8_t* w = reinterpret_cast<uint8_t*>(((uintptr_t)workspace + 1023) & ~(uintptr_t)1023);
   cudaError_t e = cudaSuccess;
   if (!r.ids.empty()) {
-    e = run_prefill(b, (int)r.ids.size(), r.ids.data(), r.nq.data(), r.kv.data(), r.decode ? kDecodeRows : 0,
+    e = run_prefill(b, (int)r.ids.size(), r.ids.data(), r.nq.data(), r.kv.data(), r.decode ? decode_row_cap(b) : 0,
                     w + align_up(dec), align_up(pre), stream);
     if (e != cudaSuccess) return e;
   }

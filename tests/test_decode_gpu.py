@@ -60,11 +60,14 @@ def test_direct_decode_formats(v_fmt, qdt):
     assert_close(to_np(out), case.oracle_bhsd(qn, tag), what=f"{v_fmt}/{qdt}")
 
 
-@pytest.mark.parametrize("Hq,Hkv", [(48, 8), (8, 4), (6, 1), (16, 16), (32, 32)])
-@pytest.mark.parametrize("Sq", [1, 4])
+@pytest.mark.parametrize("Hq,Hkv", [(48, 8), (8, 4), (6, 1), (16, 2), (16, 16), (32, 32)])
+@pytest.mark.parametrize("Sq", [1, 2, 3, 4, 5])
 def test_direct_decode_q8t(Hq, Hkv, Sq):
-    """Page-transposed Q8_0 V across kv-head group sizes (1, 4, 8 heads per
-    CTA and several CTAs per sequence), one and two m-tiles."""
+    """Page-transposed Q8_0 V across kv-head group sizes (1, 2, 4, 8 heads per
+    CTA and several CTAs per sequence) and 1..32 query rows per kv head: one,
+    two and three 8-row n-tiles of the transposed consumer (padding rows
+    included); above 24 rows per kv head the sequences go to the prefill
+    kernel."""
     lens = [4100, 1, 77, 2500, 16, 900]
     case = PagedCase(lens, Hkv, v_fmt="q8t", seed=Hq + Hkv + Sq)
     q = _q((len(lens), Hq, Sq, 128), torch.bfloat16, seed=Sq)
@@ -99,6 +102,22 @@ def test_direct_additive_mask():
     mask[:, :, 7] = 0.5
     out = _direct(case, q, mask=mask.to(dev))
     assert_close(to_np(out), case.oracle_bhsd(to_np(q), None, mask=to_np(mask)), what="mask")
+
+
+@pytest.mark.parametrize("Hq,Hkv,Sq", [(16, 2, 2), (6, 1, 1), (48, 8, 3)])
+def test_direct_additive_mask_q8t(Hq, Hkv, Sq):
+    """Additive mask with page-transposed Q8_0 V (transposed consumer, one to
+    three n-tiles)."""
+    lens = [300, 129, 2000]
+    case = PagedCase(lens, Hkv, v_fmt="q8t", seed=Hq + Sq)
+    q = _q((3, Hq, Sq, 128), torch.bfloat16, seed=Sq)
+    g = torch.Generator().manual_seed(7)
+    skv = case.max_blocks * 16
+    mask = torch.where(torch.rand((3, Sq, skv), generator=g) < 0.3, -65504.0, 0.0).half()
+    mask[:, :, 7] = 0.5
+    out = _direct(case, q, mask=mask.to(dev))
+    qn, tag = _qnp(q)
+    assert_close(to_np(out), case.oracle_bhsd(qn, tag, mask=to_np(mask)), what=f"mask q8t {Hq}/{Hkv}/{Sq}")
 
 
 def test_empty_and_short_sequences():
