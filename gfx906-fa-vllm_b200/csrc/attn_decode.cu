@@ -1388,6 +1388,7 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
 // shared memory.
 constexpr int kCombineMaxParts = 1024;
 constexpr int kCombineMaxW = 4;
+constexpr int kCombineRowW = 8;             // warps per row with one row per CTA
 __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams d) {
   __shared__ float cm[32];                    // per warp (rows x W <= 32): max
   __shared__ float cl[32];                    // den (relative to that max)
@@ -1419,9 +1420,12 @@ __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams
   }
   if (nsplit <= 1) return;
   const int R = nq * d.G;
-  const int W = blockDim.x / (32 * d.max_rows);         // warps per row (uniform)
+  // rows per CTA: all of them, or one per CTA (gridDim.z = rows) when there
+  // are few (kv head, sequence) pairs and each row has many partials
+  const int rpc = gridDim.z > 1 ? 1 : d.max_rows;
+  const int W = blockDim.x / (32 * rpc);                // warps per row (uniform)
   const int warp = threadIdx.x >> 5;
-  const int r = warp / W, wi = warp - r * W;
+  const int r = blockIdx.z * rpc + warp / W, wi = warp - (warp / W) * W;
   const int lane = threadIdx.x & 31;
   const bool active = r < R;
   // partial range of this warp: [s0, s1)
@@ -1772,8 +1776,13 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (d.tr || d.S_max > 1) {   // balanced split: any rank may span streams
-    const int cw = std::max(1, std::min(kCombineMaxW, 32 / d.max_rows));   // warps per row
-    decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows * cw, 0, stream>>>(d);
+    if ((int64_t)d.p.num_heads_kv * d.p.num_seqs < 2 * num_sms()) {
+      // few (head, sequence) pairs: one CTA per query row, 8 warps each
+      decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs, d.max_rows), 32 * kCombineRowW, 0, stream>>>(d);
+    } else {
+      const int cw = std::max(1, std::min(kCombineMaxW, 32 / d.max_rows));   // warps per row
+      decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows * cw, 0, stream>>>(d);
+    }
     e = cudaGetLastError();
   }
   return e;
