@@ -217,7 +217,7 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 
 constexpr float kRescaleLog2T = 6.0f;     // P <= 2^6: P * s_v stays finite in fp16 for any fp16 V
 
-template <bool MASK, int NST, int PPW, int NW, int NT>
+template <int VT, bool MASK, int NST, int PPW, int NW, int NT>
 __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_t* smem, uint64_t* full_bar,
                                                    uint64_t* empty_bar, StageMeta* meta, int warp, int lane) {
   using namespace dec;
@@ -240,6 +240,16 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
   const int hgb_k = d.HG * d.rb_k;
   const uint32_t kofA = (uint32_t)((tA >> 2) * d.kgs + (tA & 3) * hgb_k + hl * d.rb_k);
   const uint32_t kofB = (uint32_t)((tB >> 2) * d.kgs + (tB & 3) * hgb_k + hl * d.rb_k);
+  // 16-bit V rows: this lane's ldmatrix.trans row address (matrix mi = lane/8:
+  // keys of k-slots 8*(mi/2) + lane%8, dims 8*(mi%2) .. +7 of an m-tile)
+  uint32_t vkoff = 0;
+  if constexpr (VT <= 1) {
+    const int mi = lane >> 3, ri = lane & 7;
+    const int q = ri >> 1, e = ri & 1;
+    const uint32_t tqv = (d.tr_tab >> (8 * q)) & 0xffu;
+    const int key = 4 * q + (int)((tqv >> ((mi >> 1) ? 4 + 2 * e : 2 * e)) & 3u);
+    vkoff = (uint32_t)((key >> 1) * d.vgs + (key & 1) * d.HG * d.rb_v + hl * d.rb_v + (mi & 1) * 16);
+  }
 
   // n-tile nt holds query rows 8*nt .. 8*nt+7; this thread's accumulator
   // columns are rows 8*nt + 2*j4 + c, c = 0, 1
@@ -576,11 +586,33 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
         }
 #pragma unroll
         for (int pp = 0; pp < PPW; ++pp) {
-          pb[pp][nt][0] = movmatrix_trans(pack_half2(sacc[pp][nt][0], sacc[pp][nt][1]));
-          pb[pp][nt][1] = movmatrix_trans(pack_half2(sacc[pp][nt][2], sacc[pp][nt][3]));
+          if constexpr (VT == 1) {
+            pb[pp][nt][0] = movmatrix_trans(pack_bf162(sacc[pp][nt][0], sacc[pp][nt][1]));
+            pb[pp][nt][1] = movmatrix_trans(pack_bf162(sacc[pp][nt][2], sacc[pp][nt][3]));
+          } else {
+            pb[pp][nt][0] = movmatrix_trans(pack_half2(sacc[pp][nt][0], sacc[pp][nt][1]));
+            pb[pp][nt][1] = movmatrix_trans(pack_half2(sacc[pp][nt][2], sacc[pp][nt][3]));
+          }
         }
       }
       // ---------------- O^T += V^T P^T (V fragments shared by the n-tiles) -----
+      if constexpr (VT <= 1) {
+        // 16-bit V rows: one ldmatrix.trans per 16-dim m-tile, no conversion
+#pragma unroll
+        for (int pp = 0; pp < PPW; ++pp) {
+          const uint32_t vrow = stage_base + d.vbase + psrc[pp] * d.vps + vkoff;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt) {
+            uint32_t av[4];
+            ldmatrix_x4_trans(av, vrow + mt * 32);
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if constexpr (VT == 1) mma_bf16_16816(o[nt][mt], av, pb[pp][nt]);
+              else mma_f16_16816(o[nt][mt], av, pb[pp][nt]);
+            }
+          }
+        }
+      } else {
       const uint32_t ones = 0x3c003c00u;
 #pragma unroll
       for (int pp = 0; pp < PPW; ++pp) {
@@ -608,6 +640,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
             mma_f16_16816(corr[nt], aones, bq);
           }
         }
+      }
       }
     }
     __syncwarp();
@@ -939,8 +972,8 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
   // compute warps
   // =========================================================================
   if constexpr (TR) {
-    static_assert(VT == 3, "transposed consumer: page-transposed Q8_0 V");
-    decode_consumer_tr<MASK, NST, PPW, NWC, NT>(d, smem, full_bar, empty_bar, meta, warp, lane);
+    static_assert(VT != 2, "transposed consumer: 16-bit V rows or page-transposed Q8_0 V");
+    decode_consumer_tr<VT, MASK, NST, PPW, NWC, NT>(d, smem, full_bar, empty_bar, meta, warp, lane);
   } else {
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_COMPUTE));
   const int hl = warp % d.HG;       // local kv head
@@ -1505,9 +1538,13 @@ static int num_sms() {
 // k-slots (2j, 2j+1).  Chosen to minimise shared-memory wavefronts of the K
 // fragment loads (8 rows x 4 lanes per instruction, 2-byte loads) for the
 // launch's K row addresses.
-static uint32_t search_tr_table(int kgs, int hgb_k) {
+// vgs > 0: 16-bit V rows in 2-token groups (vgs bytes, rows hgb_v apart),
+// read by ldmatrix.trans 8 keys at a time; their 16-byte rows should fall in
+// 8 different bank groups as well.
+static uint32_t search_tr_table(int kgs, int hgb_k, int vgs, int hgb_v) {
   using namespace dec;
   auto kaddr = [&](int key) { return (key >> 2) * kgs + (key & 3) * hgb_k; };
+  auto vaddr = [&](int key) { return (key >> 1) * vgs + (key & 1) * hgb_v; };
   static const int pairs[6][4] = {{0, 1, 2, 3}, {0, 2, 1, 3}, {0, 3, 1, 2}, {1, 2, 0, 3}, {1, 3, 0, 2}, {2, 3, 0, 1}};
   auto wavefronts = [](const int* addr, int n) {   // 4-byte banks; same word is a broadcast
     int words[32][32], cnt[32] = {0}, worst = 0;
@@ -1541,6 +1578,15 @@ static uint32_t search_tr_table(int kgs, int hgb_k) {
         for (int l = 0; l < 32; ++l) a[l] = rows[l >> 2] + blk * QBLOCK;
         cost += wavefronts(a, 32);
       }
+      if (vgs > 0) {      // 16 ldmatrix phases per page and half
+        int cnt[8] = {0}, worst = 0;
+        for (int rq = 0; rq < 8; ++rq) {
+          const int q = rq >> 1;
+          const int g = (vaddr(4 * q + pairs[sel[q]][2 * half + (rq & 1)]) >> 4) & 7;
+          worst = std::max(worst, ++cnt[g]);
+        }
+        cost += 16 * worst;
+      }
     }
     if (cost < best_cost) {
       best_cost = cost;
@@ -1557,16 +1603,19 @@ static uint32_t search_tr_table(int kgs, int hgb_k) {
 // The search depends only on the K row geometry; results are cached (a few
 // layouts per process).
 static uint32_t choose_tr_table(const DecodeParams& d) {
-  struct Entry { int kgs, hgb_k; uint32_t tab; };
+  struct Entry { int kgs, hgb_k, vgs, hgb_v; uint32_t tab; };
   static Entry cache[16];
   static int n = 0;
   static std::mutex mu;
   const int hgb_k = d.HG * d.rb_k;
+  const bool v16 = d.p.v_fmt == G9_VFMT_F16 || d.p.v_fmt == G9_VFMT_BF16;
+  const int vgs = v16 ? d.vgs : 0, hgb_v = v16 ? d.HG * d.rb_v : 0;
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < n; ++i)
-    if (cache[i].kgs == d.kgs && cache[i].hgb_k == hgb_k) return cache[i].tab;
-  const uint32_t tab = search_tr_table(d.kgs, hgb_k);
-  if (n < 16) cache[n++] = Entry{d.kgs, hgb_k, tab};
+    if (cache[i].kgs == d.kgs && cache[i].hgb_k == hgb_k && cache[i].vgs == vgs && cache[i].hgb_v == hgb_v)
+      return cache[i].tab;
+  const uint32_t tab = search_tr_table(d.kgs, hgb_k, vgs, hgb_v);
+  if (n < 16) cache[n++] = Entry{d.kgs, hgb_k, vgs, hgb_v, tab};
   return tab;
 }
 
@@ -1585,7 +1634,7 @@ static bool decode_tr_enabled() {
 int decode_row_cap(const G9AttnBatch& p) {
   const int G = p.num_heads_kv > 0 ? p.num_heads_q / p.num_heads_kv : 0;
   const int HG = p.num_heads_kv % 8 == 0 ? 8 : (p.num_heads_kv % 4 == 0 ? 4 : (p.num_heads_kv % 2 == 0 ? 2 : 1));
-  const bool tr = p.v_fmt == G9_VFMT_Q8T && G >= 1 && G <= 24 && p.num_heads_kv > 0 &&
+  const bool tr = (p.v_fmt == G9_VFMT_Q8T || p.v_fmt == G9_VFMT_F16 || p.v_fmt == G9_VFMT_BF16) && G >= 1 && G <= 24 && p.num_heads_kv > 0 &&
                   (int64_t)p.num_seqs * (p.num_heads_kv / HG) <= dec::kMaxRanksTR && decode_tr_enabled();
   return tr ? 24 : 32;
 }
@@ -1667,8 +1716,9 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // transposed consumer: up to 3 n-tiles of 8 query rows; 16 compute warps
   // only for one n-tile and one kv head per CTA (register budget)
   d.nt = (R + 7) / 8;
-  d.tr = vq8t && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled()
-             ? (d.HG == 1 && d.nt == 1 ? NWC_TR : NWC) : 0;
+  const bool v16 = p.v_fmt == G9_VFMT_F16 || p.v_fmt == G9_VFMT_BF16;
+  d.tr = (vq8t || v16) && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled()
+             ? (vq8t && d.HG == 1 && d.nt == 1 ? NWC_TR : NWC) : 0;
   const int nwc = d.tr ? d.tr : NWC;
   d.P = nwc / d.HG;
   d.NG = nwc / d.HG;
@@ -1682,7 +1732,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
   // (one m-tile only: with two the registers would spill); else one page per
   // warp with 4 stages, or 3 when 4 do not fit.
-  if (d.tr != NWC_TR && (d.tr ? d.nt == 1 : mt == 1) && 2 * d.P <= 8 && need(3, 2 * d.P) <= kSmem) {
+  if (d.tr != NWC_TR && (d.tr ? d.nt == 1 && vq8t : mt == 1) && 2 * d.P <= 8 && need(3, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = 3;
@@ -1761,12 +1811,20 @@ static cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
         kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC, 2> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC, 2>;
       }
     }
-  } else if constexpr (VT == 3) {
+  } else if constexpr (VT != 2) {
     if (d.tr) {
       if (d.nt == 3)
-        kern = d.nst == 4 ? decode_kernel<2, 3, MASK, 4, 1, dec::NWC, 3> : decode_kernel<2, 3, MASK, 3, 1, dec::NWC, 3>;
+        kern = d.nst == 4 ? decode_kernel<2, VT, MASK, 4, 1, dec::NWC, 3> : decode_kernel<2, VT, MASK, 3, 1, dec::NWC, 3>;
       else
-        kern = d.nst == 4 ? decode_kernel<2, 3, MASK, 4, 1, dec::NWC, 2> : decode_kernel<2, 3, MASK, 3, 1, dec::NWC, 2>;
+        kern = d.nst == 4 ? decode_kernel<2, VT, MASK, 4, 1, dec::NWC, 2> : decode_kernel<2, VT, MASK, 3, 1, dec::NWC, 2>;
+    }
+  }
+  if constexpr (MT == 1 && VT <= 1) {
+    if (d.tr) {
+      if (d.nt == 1)
+        kern = d.nst == 4 ? decode_kernel<1, VT, MASK, 4, 1, dec::NWC, 1> : decode_kernel<1, VT, MASK, 3, 1, dec::NWC, 1>;
+      else
+        kern = d.nst == 4 ? decode_kernel<1, VT, MASK, 4, 1, dec::NWC, 2> : decode_kernel<1, VT, MASK, 3, 1, dec::NWC, 2>;
     }
   }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
