@@ -58,7 +58,8 @@ constexpr int NWC_TR = 16;
 constexpr int NTHREADS_TR = 640;
 constexpr int REG_COMPUTE_TR = 104;
 constexpr int REG_PRODUCER_TR = 64;
-constexpr int kMaxRanksTR = 4095;           // (sequence, head group) pairs: prefix sums in shared memory
+constexpr int kMaxRanksTR = 4095;
+constexpr int kVgtSmallHG = 8;              // 16-bit V tokens per copy group at 1-2 heads per CTA (measured: 2, 4, 8, 16 -> 8 best)           // (sequence, head group) pairs: prefix sums in shared memory
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*224 + 128*56 (the producer's
 // per-group stream state needs 56 to stay out of local memory)
@@ -82,7 +83,8 @@ struct DecodeParams {
   int rb_k, rb_v;         // bytes of one K / V row
   int vrec;               // page-transposed Q8_0 V: bytes of one (page, head) record
   int vrec_contig;        // 1: the records of a CTA's kv heads are adjacent (one copy per page)
-  int kgs, vgs;           // smem bytes per K group (4 tokens) / V group (2 tokens), padded to odd x 16
+  int kgs, vgs;           // smem bytes per K group (4 tokens) / V group (vgt tokens), padded to odd x 16
+  int vgt;                // 16-bit V: tokens per shared-memory group
   int contig;             // 1: rows of consecutive tokens are adjacent (one copy per group)
   int kwhole;             // 1: a page's K rows are one copy into an unpadded shared-memory page
   int cps_log2;           // log2 of the producer's copy slots per page (2..32 slots)
@@ -248,7 +250,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
     const int q = ri >> 1, e = ri & 1;
     const uint32_t tqv = (d.tr_tab >> (8 * q)) & 0xffu;
     const int key = 4 * q + (int)((tqv >> ((mi >> 1) ? 4 + 2 * e : 2 * e)) & 3u);
-    vkoff = (uint32_t)((key >> 1) * d.vgs + (key & 1) * d.HG * d.rb_v + hl * d.rb_v + (mi & 1) * 16);
+    vkoff = (uint32_t)((key / d.vgt) * d.vgs + (key % d.vgt) * d.HG * d.rb_v + hl * d.rb_v + (mi & 1) * 16);
   }
 
   // n-tile nt holds query rows 8*nt .. 8*nt+7; this thread's accumulator
@@ -934,9 +936,9 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
             continue;
           }
         }
-        if (!isk && q >= (d.contig ? 8 : 16)) continue;
+        if (!isk && q >= (d.contig ? PAGE / d.vgt : 16)) continue;
         const int hgb = isk ? hgb_k : hgb_v;
-        const int gt = isk ? (d.kwhole ? PAGE : 4) : 2;   // tokens per copy
+        const int gt = isk ? (d.kwhole ? PAGE : 4) : d.vgt;   // tokens per copy
         const uint8_t* src = (isk ? p.k_cache : p.v_cache) +
                              (int64_t)phys_j * (isk ? p.k_page_stride : p.v_page_stride) +
                              (int64_t)h0 * (isk ? p.k_head_stride : p.v_head_stride);
@@ -1538,13 +1540,13 @@ static int num_sms() {
 // k-slots (2j, 2j+1).  Chosen to minimise shared-memory wavefronts of the K
 // fragment loads (8 rows x 4 lanes per instruction, 2-byte loads) for the
 // launch's K row addresses.
-// vgs > 0: 16-bit V rows in 2-token groups (vgs bytes, rows hgb_v apart),
+// vgs > 0: 16-bit V rows in vgt-token groups (vgs bytes, rows hgb_v apart),
 // read by ldmatrix.trans 8 keys at a time; their 16-byte rows should fall in
 // 8 different bank groups as well.
-static uint32_t search_tr_table(int kgs, int hgb_k, int vgs, int hgb_v) {
+static uint32_t search_tr_table(int kgs, int hgb_k, int vgs, int hgb_v, int vgt) {
   using namespace dec;
   auto kaddr = [&](int key) { return (key >> 2) * kgs + (key & 3) * hgb_k; };
-  auto vaddr = [&](int key) { return (key >> 1) * vgs + (key & 1) * hgb_v; };
+  auto vaddr = [&](int key) { return (key / vgt) * vgs + (key % vgt) * hgb_v; };
   static const int pairs[6][4] = {{0, 1, 2, 3}, {0, 2, 1, 3}, {0, 3, 1, 2}, {1, 2, 0, 3}, {1, 3, 0, 2}, {2, 3, 0, 1}};
   auto wavefronts = [](const int* addr, int n) {   // 4-byte banks; same word is a broadcast
     int words[32][32], cnt[32] = {0}, worst = 0;
@@ -1603,7 +1605,7 @@ static uint32_t search_tr_table(int kgs, int hgb_k, int vgs, int hgb_v) {
 // The search depends only on the K row geometry; results are cached (a few
 // layouts per process).
 static uint32_t choose_tr_table(const DecodeParams& d) {
-  struct Entry { int kgs, hgb_k, vgs, hgb_v; uint32_t tab; };
+  struct Entry { int kgs, hgb_k, vgs, hgb_v, vgt; uint32_t tab; };
   static Entry cache[16];
   static int n = 0;
   static std::mutex mu;
@@ -1612,10 +1614,11 @@ static uint32_t choose_tr_table(const DecodeParams& d) {
   const int vgs = v16 ? d.vgs : 0, hgb_v = v16 ? d.HG * d.rb_v : 0;
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < n; ++i)
-    if (cache[i].kgs == d.kgs && cache[i].hgb_k == hgb_k && cache[i].vgs == vgs && cache[i].hgb_v == hgb_v)
+    if (cache[i].kgs == d.kgs && cache[i].hgb_k == hgb_k && cache[i].vgs == vgs && cache[i].hgb_v == hgb_v &&
+        cache[i].vgt == d.vgt)
       return cache[i].tab;
-  const uint32_t tab = search_tr_table(d.kgs, hgb_k, vgs, hgb_v);
-  if (n < 16) cache[n++] = Entry{d.kgs, hgb_k, vgs, hgb_v, tab};
+  const uint32_t tab = search_tr_table(d.kgs, hgb_k, vgs, hgb_v, d.vgt);
+  if (n < 16) cache[n++] = Entry{d.kgs, hgb_k, vgs, hgb_v, d.vgt, tab};
   return tab;
 }
 
@@ -1700,18 +1703,6 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // removes them and the rows are copied in 4-token groups.
   d.kwhole = d.contig && d.HG <= 2;
   if (d.kwhole) d.kgs = 4 * hgk;
-  {
-    const int kc = d.kwhole ? 1 : (d.contig ? 4 : 16);
-    const int vc = vq8t ? (d.vrec_contig ? 1 : d.HG) : (d.contig ? 8 : 16);
-    int l = 1;
-    while ((1 << l) < kc + vc) ++l;
-    d.cps_log2 = l;                       // 2 .. 32 slots
-  }
-  d.vgs = pad_odd16(2 * hgv);
-  d.kpage = (PAGE / 4) * d.kgs;
-  // page-transposed V: the HG records back to back (ldmatrix rows are 16
-  // consecutive bytes, conflict-free at any 16-byte aligned base)
-  d.vpage = vq8t ? d.HG * d.vrec : (PAGE / 2) * d.vgs;
   d.nranks = p.num_seqs * d.HGN;
   // transposed consumer: up to 3 n-tiles of 8 query rows; 16 compute warps
   // only for one n-tile and one kv head per CTA (register budget)
@@ -1719,6 +1710,28 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   const bool v16 = p.v_fmt == G9_VFMT_F16 || p.v_fmt == G9_VFMT_BF16;
   d.tr = (vq8t || v16) && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled()
              ? (vq8t && d.HG == 1 && d.nt == 1 ? NWC_TR : NWC) : 0;
+  // 16-bit V tokens per shared-memory group (one copy per group when rows are
+  // adjacent): 2, padded, for the 16-row kernel; the transposed kernel with
+  // one or two heads per CTA, where the producer's copy-request rate binds,
+  // takes larger groups (tuned below)
+  d.vgt = 2;
+  if (d.tr && v16 && d.contig && d.HG <= 2) d.vgt = kVgtSmallHG;
+  if (const char* e = std::getenv("GFX906_FA_DECODE_VGT")) {      // tuning override
+    const int v = std::atoi(e);
+    if (d.tr && v16 && d.contig && (v == 2 || v == 4 || v == 8 || v == 16)) d.vgt = v;
+  }
+  {
+    const int kc = d.kwhole ? 1 : (d.contig ? 4 : 16);
+    const int vc = vq8t ? (d.vrec_contig ? 1 : d.HG) : (d.contig ? PAGE / d.vgt : 16);
+    int l = 1;
+    while ((1 << l) < kc + vc) ++l;
+    d.cps_log2 = l;                       // 2 .. 32 slots
+  }
+  d.vgs = pad_odd16(d.vgt * hgv);
+  d.kpage = (PAGE / 4) * d.kgs;
+  // page-transposed V: the HG records back to back (ldmatrix rows are 16
+  // consecutive bytes, conflict-free at any 16-byte aligned base)
+  d.vpage = vq8t ? d.HG * d.vrec : (PAGE / d.vgt) * d.vgs;
   const int nwc = d.tr ? d.tr : NWC;
   d.P = nwc / d.HG;
   d.NG = nwc / d.HG;
