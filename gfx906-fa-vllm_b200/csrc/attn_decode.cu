@@ -58,8 +58,9 @@ constexpr int NWC_TR = 16;
 constexpr int NTHREADS_TR = 640;
 constexpr int REG_COMPUTE_TR = 104;
 constexpr int REG_PRODUCER_TR = 64;
-constexpr int kMaxRanksTR = 4095;
-constexpr int kVgtSmallHG = 8;              // 16-bit V tokens per copy group at 1-2 heads per CTA (measured: 2, 4, 8, 16 -> 8 best)           // (sequence, head group) pairs: prefix sums in shared memory
+constexpr int kMaxRanksTR = 4095;           // (sequence, head group) pairs: prefix sums in shared memory
+// 16-bit V tokens per copy group at 1-2 heads per CTA (measured 2, 4, 8, 16: 8 fastest)
+constexpr int kVgtSmallHG = 8;
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*224 + 128*56 (the producer's
 // per-group stream state needs 56 to stay out of local memory)
