@@ -59,8 +59,10 @@ constexpr int NTHREADS_TR = 640;
 constexpr int REG_COMPUTE_TR = 104;
 constexpr int REG_PRODUCER_TR = 64;
 constexpr int kMaxRanksTR = 4095;           // (sequence, head group) pairs: prefix sums in shared memory
-// 16-bit V tokens per copy group at 1-2 heads per CTA (measured 2, 4, 8, 16: 8 fastest)
+// 16-bit V tokens per copy group of the transposed kernel, measured over
+// 2, 4, 8 (16): at 1-2 heads per CTA 8 is fastest, at 4-8 heads 4
 constexpr int kVgtSmallHG = 8;
+constexpr int kVgtLargeHG = 4;
 constexpr int QROW = 272;                   // smem bytes per Q row (256 + pad, conflict-free ldmatrix)
 // setmaxnreg split: launch 384 threads x 168 = 64512 = 256*224 + 128*56 (the producer's
 // per-group stream state needs 56 to stay out of local memory)
@@ -1712,11 +1714,11 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   d.tr = (vq8t || v16) && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled()
              ? (vq8t && d.HG == 1 && d.nt == 1 ? NWC_TR : NWC) : 0;
   // 16-bit V tokens per shared-memory group (one copy per group when rows are
-  // adjacent): 2, padded, for the 16-row kernel; the transposed kernel with
-  // one or two heads per CTA, where the producer's copy-request rate binds,
-  // takes larger groups (tuned below)
+  // adjacent): 2, padded, for the 16-row kernel; the transposed kernel takes
+  // larger groups (fewer copy requests; its key order keeps the ldmatrix
+  // reads spread over the banks as far as the layout allows)
   d.vgt = 2;
-  if (d.tr && v16 && d.contig && d.HG <= 2) d.vgt = kVgtSmallHG;
+  if (d.tr && v16 && d.contig) d.vgt = d.HG <= 2 ? kVgtSmallHG : kVgtLargeHG;
   if (const char* e = std::getenv("GFX906_FA_DECODE_VGT")) {      // tuning override
     const int v = std::atoi(e);
     if (d.tr && v16 && d.contig && (v == 2 || v == 4 || v == 8 || v == 16)) d.vgt = v;
