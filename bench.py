@@ -83,31 +83,63 @@ def config5_work(kv, nq, hkv, hq, v_row):
 # clocks sampling
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """Samples SM clocks and throttle reasons while the timed region runs:
+    NVML polled every 5 ms (so even a region of a few milliseconds gets
+    several samples), nvidia-smi every 200 ms when NVML is not importable."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, index):
         self.index = index
-        self.rows = []
+        self.rows = []           # (sm_mhz, max_mhz, set of active reason names)
         self._stop = threading.Event()
         self._t = None
 
-    def _run(self):
+    def _run_nvml(self, nv):
+        h = nv.nvmlDeviceGetHandleByIndex(self.index)
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+            bits = int(get_reasons(h))
+            self.rows.append((sm, mx, {n for n, b in self.REASONS if bits & b}))
+            self._stop.wait(0.005)
+
+    def _run_smi(self):
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                                       "--format=csv,noheader,nounits"], capture_output=True, text=True,
                                      timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([x.strip() for x in out.split(",")])
+                r = [x.strip() for x in out.split(",")] if out else []
+                if len(r) >= 8 and r[1].replace(".", "").isdigit():
+                    names = [n for n, _ in self.REASONS]
+                    self.rows.append((float(r[1]), float(r[2]) if r[2].replace(".", "").isdigit() else None,
+                                      {names[i] for i in range(4) if r[4 + i] == "Active"}))
             except Exception:
                 pass
             self._stop.wait(0.2)
 
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+        except Exception:
+            self._run_smi()
+            return
+        try:
+            self._run_nvml(nv)
+        except Exception:
+            self._run_smi()
+
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
+        time.sleep(0.02)                     # first sample before the region starts
         return self
 
     def __exit__(self, *a):
@@ -117,11 +149,10 @@ class ClockSampler:
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 4 + i and r[4 + i] == "Active"})
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+        sm = [r[0] for r in self.rows]
+        mx = [r[1] for r in self.rows if r[1]]
+        reasons = sorted(set().union(*[r[2] for r in self.rows]))
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(self.rows)}
 
 
@@ -172,6 +203,13 @@ def build_cache(lens, hkv, seed, device, v_fmt="fp16"):
 # 21.81 MB against 462.36 MB of algorithmic bytes; fp16 V read 666.97 MB and
 # wrote 20.39 MB against 666.14 MB.  The writes are the split-K partials.
 DECODE_TRAFFIC_RATIO = {"q8_0": (462.63 + 5.18) / 462.36, "fp16": (666.54 + 5.09) / 666.14}
+
+
+# DRAM bytes (read + write) per FLOP of prefill_kernel, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of the last 8192-query chunk
+# of the 32K prefill; None until measured.
+PREFILL_TRAFFIC_PER_FLOP = None
+PREFILL_TRAFFIC_NOTE = "not captured"
 
 
 def decode_bytes(lens, hkv, hq, v_row=256):
@@ -234,6 +272,60 @@ def cpu_baseline(seconds_target=10.0, threads=None, v_fmt="q8_0"):
                       f"oracle/q8_oracle.c attention, OpenMP"}, elapsed
 
 
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def torch_cpu_baseline(seconds_target=10.0, v_fmt="q8_0"):
+    """The reference's own torch CPU pipeline (restated in
+    oracle/torch_path.py: page gather by fancy indexing, dequantize_q8_0,
+    repeat_interleave for GQA, torch SDPA in fp32) over the config-3
+    sequences until ~seconds_target of work, with torch's full host thread
+    pool.  Returns GB/s in the decode metric's bytes."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch_path as TP
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    lens = config3_lens()
+    g = torch.Generator().manual_seed(0)
+    done_bytes, elapsed, nseq = 0, 0.0, 0
+    for L in lens:
+        L = int(L)
+        nb = (L + BS - 1) // BS
+        kq = torch.randint(0, 256, (nb, BS, HKV, RB), generator=g, dtype=torch.uint8)
+        kq.view(-1, 34)[:, 0] = 0x00              # fp16 scale 0x2000: small, finite
+        kq.view(-1, 34)[:, 1] = 0x20
+        if v_fmt.startswith("q8_0"):
+            vc = kq.clone()
+            v_row = RB
+        else:
+            vc = torch.randn((nb, BS, HKV, D), generator=g).half()
+            v_row = 2 * D
+        q = torch.randn((1, HQ, D), generator=g).to(torch.bfloat16)
+        bt = torch.arange(nb, dtype=torch.int32).view(1, nb)
+        t0 = time.perf_counter()
+        TP.attention_varlen(q, kq, vc, bt, [L], [1], 1 / np.sqrt(D), v_q8=v_fmt.startswith("q8_0"))
+        elapsed += time.perf_counter() - t0
+        done_bytes += decode_bytes([L], HKV, HQ, v_row)
+        nseq += 1
+        if elapsed > seconds_target:
+            break
+    return {"value": done_bytes / elapsed / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"{nseq} of the 64 config-3 sequences ({done_bytes / 1e9:.2f} GB of algorithmic bytes) "
+                      "through the reference's torch CPU pipeline (gather by fancy indexing, dequantize_q8_0, "
+                      "repeat_interleave, F.scaled_dot_product_attention fp32; restated in oracle/torch_path.py)",
+            "host": {"cpu_model": cpu_model(), "os_cpu_count": os.cpu_count(),
+                     "torch_threads": torch.get_num_threads()}}, elapsed
+
+
 # ---------------------------------------------------------------------------
 def main():
     ap = argparse.ArgumentParser()
@@ -248,6 +340,8 @@ def main():
     ap.add_argument("--decode-seqs", type=int, default=64,
                     help="first N sequences of config 3 (profiling uses a smaller case)")
     ap.add_argument("--prefill-tokens", type=int, default=32768)
+    ap.add_argument("--prefill-long", default="65536,130000,133120",
+                    help="extra config-4 context lengths timed after the headline 32K (comma list, '' for none)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-mixed", action="store_true", help="skip the config-5 mixed-batch measurement")
     ap.add_argument("--no-kv", action="store_true", help="skip the config-2 KV store + gather measurement")
@@ -260,7 +354,9 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        res, el = cpu_baseline(seconds_target=max(3.0, min(20.0, 2.0 * args.steps)), v_fmt=args.v_fmt)
+        budget = max(3.0, min(20.0, 2.0 * args.steps))
+        res, el = torch_cpu_baseline(seconds_target=budget, v_fmt=args.v_fmt)
+        res_c, _ = cpu_baseline(seconds_target=budget / 2, v_fmt=args.v_fmt)
         line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
@@ -269,6 +365,7 @@ def main():
                                        + ("Q8_0 V" if args.v_fmt.startswith("q8_0") else "fp16 V") + ")",
                            "sample": res["sample"]},
                 "cpu_baseline": res,
+                "cpu_baseline_c_oracle": res_c,
                 "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return
@@ -436,12 +533,12 @@ def main():
         del k2, v2, bt2
         torch.cuda.empty_cache()
 
-    # ---------------- prefill (config 4 at 32K) -----------------------------
-    prefill = None
-    if not args.no_prefill:
-        N, C = args.prefill_tokens, 8192
-        del k_cache, v_cache
-        torch.cuda.empty_cache()
+    # ---------------- prefill (config 4 at 32K, 64K, 130K) ---------------------
+    def prefill_run(N, C=8192, psteps=3):
+        """One sequence of N tokens prefilled in 8192-query chunks, each chunk
+        one paged_attention call against every earlier key (causal inside the
+        chunk).  Returns (ms per prefill, staging workspace bytes of the last
+        chunk)."""
         kc, vc, btp = build_cache([N], hkv, seed=2000 + rank, device=device, v_fmt=args.v_fmt)
         qp = torch.randn((N, hq, D), generator=gq, device=device).to(torch.bfloat16)
         op = torch.empty_like(qp)
@@ -459,7 +556,6 @@ def main():
         for _ in range(max(3, args.warmup // 2)):
             prefill_step()
         barrier()
-        psteps = max(3, args.steps // 4)
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p0.record()
         for _ in range(psteps):
@@ -467,22 +563,46 @@ def main():
         p1.record()
         barrier()
         pms = max_over_ranks(p0.elapsed_time(p1)) / psteps
-        fl_all = prefill_flops(N, C, HQ)
-        tfs = fl_all / (pms * 1e-3) / 1e12
-        prefill = {"value": tfs, "unit": "TFLOP/s", "ms_per_step": pms,
+        # staging: fp16 Q rows (row tiles padded to pairs), K rows and V^T tiles of every visible key
+        s0, n = chunks[-1][0], chunks[-1][1]
+        rt = 2 * ((n * (hq // hkv) + 255) // 256)
+        kt = (s0 + n + 127) // 128
+        ws = hkv * (rt + 2 * kt) * 128 * D * 2
+        del kc, vc, btp, qp, op
+        torch.cuda.empty_cache()
+        return pms, ws, len(chunks)
+
+    prefill = None
+    if not args.no_prefill:
+        del k_cache, v_cache
+        torch.cuda.empty_cache()
+        N = args.prefill_tokens
+        pms, ws, nch = prefill_run(N, psteps=max(3, args.steps // 4))
+        fl_all = prefill_flops(N, 8192, HQ)
+        ach = fl_all / world / (pms * 1e-3) / 1e12
+        prefill = {"value": fl_all / (pms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": pms,
                    "workload": f"config4: 1 seq x {N} tokens, 8192-query chunks, causal, GQA 48/8, "
                                f"{'Q8_0' if args.v_fmt.startswith('q8_0') else 'fp16'} V",
-                   "roofline": {"bound": "tensor", "achieved": fl_all / world / (pms * 1e-3) / 1e12,
-                                "peak": tf_peak, "unit": "TFLOP/s",
-                                "frac": fl_all / world / (pms * 1e-3) / 1e12 / tf_peak,
-                                "peak_kind": f"{peak_kind} bf16 burst"},
-                   "gpu_launches_per_step": 3 * len(chunks)}
+                   "workspace_bytes": ws,
+                   "roofline": {"bound": "tensor", "achieved": ach, "peak": tf_peak, "unit": "TFLOP/s",
+                                "frac": ach / tf_peak, "peak_kind": f"{peak_kind} bf16 burst",
+                                "traffic": (PREFILL_TRAFFIC_PER_FLOP * fl_all / world
+                                            if PREFILL_TRAFFIC_PER_FLOP else None),
+                                "traffic_note": PREFILL_TRAFFIC_NOTE},
+                   "gpu_launches_per_step": 3 * nch}
+        longer = []
+        for NL in [int(x) for x in args.prefill_long.split(",") if x.strip()]:
+            lms, lws, _ = prefill_run(NL, psteps=2)
+            fl = prefill_flops(NL, 8192, HQ)
+            longer.append({"tokens": NL, "value": fl / (lms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                           "ms_per_step": lms, "tflop": fl / 1e12, "workspace_bytes": lws,
+                           "frac": fl / world / (lms * 1e-3) / 1e12 / tf_peak})
+        if longer:
+            prefill["longer_contexts"] = longer
 
     # ---------------- mixed serving batch (config 5) -------------------------
     mixed = None
     if not args.no_mixed:
-        if prefill is not None:
-            del kc, vc, btp, qp, op
         torch.cuda.empty_cache()
         kv5, nq5 = config5_batch()
         k5, v5, bt5 = build_cache(kv5, hkv, seed=4000 + rank, device=device, v_fmt=args.v_fmt)
@@ -571,9 +691,10 @@ def main():
         del k2v, v2v, key2, val2, kout, vout
         torch.cuda.empty_cache()
 
-    cpu = None
+    cpu = cpu_c = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu, _ = cpu_baseline(seconds_target=10.0, v_fmt=args.v_fmt)
+        cpu, _ = torch_cpu_baseline(seconds_target=10.0, v_fmt=args.v_fmt)
+        cpu_c, _ = cpu_baseline(seconds_target=5.0, v_fmt=args.v_fmt)
 
     if rank == 0:
         line = {
@@ -609,6 +730,8 @@ def main():
             line["prefill"] = prefill
         if cpu:
             line["cpu_baseline"] = cpu
+        if cpu_c:
+            line["cpu_baseline_c_oracle"] = cpu_c
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()

@@ -17,16 +17,77 @@ __device__ __forceinline__ int64_t o_offset(const G9AttnBatch& p, int b, int t, 
   const int qs = p.q_start ? p.q_start[b] : 0;
   return (int64_t)b * p.o_seq_stride + (int64_t)(qs + t) * p.o_tok_stride + (int64_t)hq * p.o_head_stride;
 }
-__device__ __forceinline__ int seq_nq(const G9AttnBatch& p, int b) { return p.n_q ? p.n_q[b] : p.seq_q; }
+__device__ __forceinline__ int seq_nq(const G9AttnBatch& p, int b) {
+  if (p.n_q) return p.n_q[b];
+  if (p.flags & G9_F_CU_SEQLENS) return p.q_start[b + 1] - p.q_start[b];
+  return p.seq_q;
+}
+// a causal rule is in force (per-sequence q_abs given, or the chunk ends at the last key)
+__device__ __forceinline__ bool has_causal(const G9AttnBatch& p) {
+  return p.q_abs != nullptr || (p.flags & G9_F_CAUSAL_END);
+}
+
+// Keys of sequence b: kv_len[b] clamped to what the block table can address
+// and to the host bound max_kv the launch was planned with, so a kv_len
+// beyond either never reads past the sequence's block-table row or a
+// workspace sized from max_kv.
+__device__ __forceinline__ int seq_len_kv(const G9AttnBatch& p, int b) {
+  int64_t L = p.kv_len[b];
+  const int64_t cap = (int64_t)p.max_blocks * p.block_size;
+  if (L > cap) L = cap;
+  if (L > p.max_kv) L = p.max_kv;
+  return L < 0 ? 0 : (int)L;
+}
+
+// Position of query token 0 of sequence b (token t sits at qpos0 + t): q_abs,
+// or the chunk ending at the last key.  L = seq_len_kv(p, b).
+__device__ __forceinline__ int64_t seq_qpos0(const G9AttnBatch& p, int b, int nq, int L) {
+  return p.q_abs ? (int64_t)p.q_abs[b] : (int64_t)L - nq;
+}
+// causal offset of sequence b (0 when has_causal is false)
+__device__ __forceinline__ int seq_qabs(const G9AttnBatch& p, int b, int nq, int L) {
+  return p.q_abs ? p.q_abs[b] : ((p.flags & G9_F_CAUSAL_END) ? L - nq : 0);
+}
 
 // Number of keys any query of sequence b can see (exclusive end).
 __device__ __forceinline__ int seq_kv_end(const G9AttnBatch& p, int b, int nq) {
-  int end = p.kv_len[b];
-  if (p.q_abs) {
-    const int64_t lim = (int64_t)p.q_abs[b] + nq;      // last token sees keys <= q_abs + nq - 1
+  int end = seq_len_kv(p, b);
+  if (has_causal(p)) {
+    const int64_t lim = (int64_t)seq_qabs(p, b, nq, end) + nq;   // last token sees keys <= q_abs + nq - 1
     if (lim < end) end = lim < 0 ? 0 : (int)lim;
   }
   return end;
+}
+
+// First key any query of sequence b can see: 0, or with a sliding window
+// the first key inside token 0's window (key k is visible to position qp iff
+// qp - k < window).
+__device__ __forceinline__ int seq_kv_begin(const G9AttnBatch& p, int b, int nq) {
+  if (p.window <= 0) return 0;
+  const int64_t lo = seq_qpos0(p, b, nq, seq_len_kv(p, b)) - p.window + 1;
+  return lo < 0 ? 0 : (lo > 0x7fffffff ? 0x7fffffff : (int)lo);
+}
+
+// Lower visibility limit of query token t (keys k >= the value are inside its
+// window); INT_MIN without a window.
+__device__ __forceinline__ int window_lo(const G9AttnBatch& p, int64_t qpos0, int t) {
+  if (p.window <= 0) return -0x7fffffff - 1;
+  const int64_t lo = qpos0 + t - p.window + 1;
+  return lo < -0x7fffffff ? -0x7fffffff : (lo > 0x7fffffff ? 0x7fffffff : (int)lo);
+}
+
+// A block-table entry that must not be dereferenced.
+__device__ __forceinline__ bool page_bad(const G9AttnBatch& p, int phys) {
+  return phys < 0 || (p.num_blocks > 0 && phys >= p.num_blocks);
+}
+
+// Soft-capped score in log2 units: cap * tanh(raw * scale / cap) * log2(e),
+// with in = scale / cap and out = cap * log2(e) precomputed on the host.
+__device__ __forceinline__ float softcap_log2(float raw, float in, float out) { return out * tanhf(raw * in); }
+
+// Sink of query head hq in log2 units (0 weight when there is none).
+__device__ __forceinline__ float sink_log2(const G9AttnBatch& p, int hq) {
+  return p.sinks ? p.sinks[hq] * 1.4426950408889634f : -INFINITY;
 }
 
 __device__ __forceinline__ void store_out2(void* out, int dt, int64_t off, float a, float b) {

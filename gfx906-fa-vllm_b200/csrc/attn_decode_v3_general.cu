@@ -1,0 +1,9 @@
+// attn_decode_v3_general.cu -- decode launcher for page-transposed Q8_0 V, general score path (mask / soft-cap / window).
+#include "attn_decode_kern.cuh"
+
+namespace g9 {
+template cudaError_t launch_decode_t<1, 3, true>(const DecodeParams&, cudaStream_t);
+template cudaError_t launch_decode_t<2, 3, true>(const DecodeParams&, cudaStream_t);
+}  // namespace g9
+
+G9_ERROR_ACCESSORS(decode_v3g)

@@ -74,6 +74,7 @@ struct PrefillParams {
   int rtile_off[pf::MAXS + 1];
   int ktile_off[pf::MAXS + 1];
   float scale_log2;
+  float cap_in, cap_out;         // soft-cap: scale / softcap and softcap * log2(e) (softcap > 0)
   __half* qp;                    // [Hkv][RT*128][128]
   __half* kp;                    // [Hkv][KT*128][128]
   __half* vt;                    // [Hkv][KT][128 d][128 keys]: V^T tiles
@@ -102,8 +103,10 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
   const int i = find_seq(pp.ktile_off, pp.nseq, kt);
   const int j = kt - pp.ktile_off[i];
   const int b = pp.seq_b[i];
-  if (seq_nq(p, b) * pp.G <= pp.min_rows) return;      // handled by the decode kernel
-  const int L = p.kv_len[b];
+  const int nq = seq_nq(p, b);
+  if (nq * pp.G <= pp.min_rows) return;                // handled by the decode kernel
+  const int L = min(seq_len_kv(p, b), (pp.ktile_off[i + 1] - pp.ktile_off[i]) * BN);
+  if ((j + 1) * BN <= seq_kv_begin(p, b, nq)) return;  // before every row's window: never read
   __half* kdst = pp.kp + ((int64_t)h * pp.KT + kt) * BN * D;
   for (int it = threadIdx.x; it < BN * 8; it += blockDim.x) {
     const int key_l = it >> 3;
@@ -111,11 +114,12 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
     const int key = j * BN + key_l;
     __align__(16) __half kv[16];
     __align__(16) __half vv[16];
-    if (key < L) {
-      const int phys = p.block_table[(int64_t)b * p.max_blocks + key / p.block_size];
-      if (phys < 0) raise_error(ERR_BAD_PAGE);
+    const int phys = key < L ? p.block_table[(int64_t)b * p.max_blocks + key / p.block_size] : -1;
+    const bool bad = key < L && page_bad(p, phys);
+    if (bad && c == 0) raise_error(ERR_BAD_PAGE);      // its keys are packed as zero vectors
+    if (key < L && !bad) {
       const int64_t off_t = (int64_t)(key % p.block_size);
-      const uint8_t* krow = p.k_cache + (int64_t)max(phys, 0) * p.k_page_stride + off_t * p.k_tok_stride +
+      const uint8_t* krow = p.k_cache + (int64_t)phys * p.k_page_stride + off_t * p.k_tok_stride +
                             (int64_t)h * p.k_head_stride;
       const uint8_t* kb = krow + (c >> 1) * QBLOCK;
       const float dk = __half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(kb)));
@@ -126,12 +130,12 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
         kv[2 * e] = __float2half_rn((float)(int8_t)(w & 0xff) * dk);
         kv[2 * e + 1] = __float2half_rn((float)(int8_t)(w >> 8) * dk);
       }
-      const uint8_t* vrow = p.v_cache + (int64_t)max(phys, 0) * p.v_page_stride + off_t * p.v_tok_stride +
+      const uint8_t* vrow = p.v_cache + (int64_t)phys * p.v_page_stride + off_t * p.v_tok_stride +
                             (int64_t)h * p.v_head_stride;
       if (p.v_fmt == G9_VFMT_Q8T) {
         // page-transposed record: scale (block j, token t) at 2*(j*bs + t),
         // int8 (dim, token t) at 2*(D/32)*bs + dim*bs + t
-        const uint8_t* rec = p.v_cache + (int64_t)max(phys, 0) * p.v_page_stride + (int64_t)h * p.v_head_stride;
+        const uint8_t* rec = p.v_cache + (int64_t)phys * p.v_page_stride + (int64_t)h * p.v_head_stride;
         const int bsz = p.block_size;
         const float dv = __half2float(__ushort_as_half(
             *reinterpret_cast<const uint16_t*>(rec + 2 * ((int64_t)(c >> 1) * bsz + off_t))));
@@ -418,17 +422,22 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   const int b = pp.seq_b[si];
   const int nq = seq_nq(p, b);
   const int R = nq * pp.G;
-  const int kv_len = p.kv_len[b];
-  const int qabs = p.q_abs ? p.q_abs[b] : 0;
+  // keys of the sequence, clamped also to the staging tiles its kv bound sized
+  const int kv_len = min(seq_len_kv(p, b), (pp.ktile_off[si + 1] - pp.ktile_off[si]) * BN);
+  const int qabs = seq_qabs(p, b, nq, kv_len);
+  const bool causal = has_causal(p);
   const int row0 = m * BM;
   if (row0 >= R || R <= pp.min_rows) return;              // padding pair / decode-sized sequence
   const bool has1 = row0 + BM < R;                         // second tile holds rows
   const int t_hi = min(nq - 1, (row0 + 2 * BM - 1) / pp.G);
   int key_end = kv_len;                                    // keys any row of the pair sees
-  if (p.q_abs) key_end = min(key_end, max(0, qabs + t_hi + 1));
-  const int nkv = (key_end + BN - 1) / BN;
+  if (causal) key_end = min(key_end, max(0, qabs + t_hi + 1));
+  const int64_t qpos0 = seq_qpos0(p, b, nq, kv_len);
+  // sliding window: key tiles before the first row's window are skipped
+  const int j0 = min(max(window_lo(p, qpos0, row0 / pp.G), 0) / BN, (key_end + BN - 1) / BN);
+  const int nkv = (key_end + BN - 1) / BN - j0;           // key tiles j0 .. j0 + nkv - 1
   const int q_row_g = (h * pp.RT + grt) * BM;
-  const int k_row_g = (h * pp.KT + pp.ktile_off[si]) * BN;
+  const int k_row_g = (h * pp.KT + pp.ktile_off[si] + j0) * BN;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_q, 1);
@@ -463,7 +472,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         if (j >= KST && !mbar_wait(&bar_kempty[ks], ((j / KST) - 1) & 1)) { abort_flag = 1; break; }
         uint8_t* kd = sK + ks * TILE_BYTES;
         mbar_arrive_expect_tx(&bar_kfull[ks], TILE_BYTES);
-        tma_load_2d(kd, &pp.tm_k, 0, k_row_g + j * BN, &bar_kfull[ks]);
+        tma_load_2d(kd, &pp.tm_k, 0, k_row_g + j * BN, &bar_kfull[ks]);   // key tile j0 + j
         tma_load_2d(kd + TILE_BYTES / 2, &pp.tm_k, 64, k_row_g + j * BN, &bar_kfull[ks]);
         const int vs = j % VST;
         if (j >= VST && !mbar_wait(&bar_vempty[vs], ((j / VST) - 1) & 1)) { abort_flag = 1; break; }
@@ -532,11 +541,12 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
     const int t = rg / pp.G;
     const bool row_valid = rg < R;
     int row_end = kv_len;                                  // keys this row sees
-    if (p.q_abs) row_end = min(row_end, max(0, qabs + t + 1));
+    if (causal) row_end = min(row_end, max(0, qabs + t + 1));
     if (!row_valid) row_end = 0;
+    const int row_lo = window_lo(p, qpos0, t);             // and its window's first key
     // keys every row of this tile sees
     int key_full = kv_len;
-    if (p.q_abs) key_full = min(key_full, max(0, qabs + (row0 + wi * BM) / pp.G + 1));
+    if (causal) key_full = min(key_full, max(0, qabs + (row0 + wi * BM) / pp.G + 1));
     const bool active = nkv > 0 && (wi == 0 || has1);
     float m_run = -INFINITY, l_run = 0.f;                  // log2 units, scale applied
     bool alive = true;
@@ -548,7 +558,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + lane_off + c * 32, s[c]);
       tmem_wait_ld();
-      const int k0 = j * BN;
+      const int k0 = (j0 + j) * BN;
       const bool need_mask = MASK || (k0 + BN > key_full) || !row_valid;
       if (need_mask) {
 #pragma unroll
@@ -556,14 +566,16 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             float x = __uint_as_float(s[c][e]);
+            const int k = k0 + c * 32 + e;
             if constexpr (MASK) {
-              x *= pp.scale_log2;
-              const int k = k0 + c * 32 + e;
+              // general scores: soft-cap, additive mask, sliding window
+              x = p.softcap > 0.f ? softcap_log2(x, pp.cap_in, pp.cap_out) : x * pp.scale_log2;
               if (p.mask && row_valid && k < kv_len)
                 x += kLog2e * __half2float(reinterpret_cast<const __half*>(p.mask)[
                     (int64_t)b * p.mask_seq_stride + (int64_t)t * p.mask_tok_stride + k]);
+              if (k < row_lo) x = -INFINITY;
             }
-            if (k0 + c * 32 + e >= row_end) x = -INFINITY;
+            if (k >= row_end) x = -INFINITY;
             s[c][e] = __float_as_uint(x);
           }
       }
@@ -648,8 +660,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
     if (active) {
       if (alive && mbar_wait(&bar_o[wi], 0)) {
         tc_fence_after();
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         const int g = rg - t * pp.G;
+        if (p.sinks && l_run > 0.f) l_run += fast_exp2(sink_log2(p, h * pp.G + g) - m_run);
+        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
         const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -766,6 +779,10 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     pp.nseq = n;
     pp.min_rows = min_rows;
     pp.scale_log2 = p.scale * kLog2e;
+    if (p.softcap > 0.f) {
+      pp.cap_in = p.scale / p.softcap;
+      pp.cap_out = p.softcap * kLog2e;
+    }
     int ro = 0, ko = 0;
     for (int i = 0; i < n; ++i) {
       pp.seq_b[i] = seq_ids[base + i];
@@ -793,7 +810,9 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     pack_q_kernel<<<dim3(pp.RT, pp.Hkv), 256, 0, stream>>>(pp);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t smem = (size_t)(2 + KST + VST) * TILE_BYTES + 1024;
-    auto kern = (p.mask || !(p.scale > 0.f)) ? prefill_kernel<true> : prefill_kernel<false>;
+    // general score path: mask, non-positive scale, soft-cap or sliding window
+    const bool general = p.mask || !(p.scale > 0.f) || p.softcap > 0.f || p.window > 0;
+    auto kern = general ? prefill_kernel<true> : prefill_kernel<false>;
     if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess)
       return e;
     kern<<<pp.Hkv * (pp.RT / 2), NTHREADS, smem, stream>>>(pp);

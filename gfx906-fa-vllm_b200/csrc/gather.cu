@@ -32,6 +32,7 @@ struct GatherArgs {
   int64_t kc_blk, kc_tok, kc_head;   // bytes
   int64_t vc_blk, vc_tok, vc_head;   // bytes
   int B, Hkv, Sk, D, rb, bs, max_blocks;
+  int num_blocks;                // > 0: entries >= num_blocks are out of range (and flagged)
   int kw;                        // K store width (2, 4 or 8 bytes)
 };
 
@@ -74,7 +75,12 @@ __global__ void __launch_bounds__(kGatherThreads) gather_kernel(GatherArgs a) {
   if (tok0 >= a.Sk) return;
   if (threadIdx.x == 0) {
     s_len = a.sl[b];
-    s_phys = page < a.max_blocks ? a.bt[(int64_t)b * a.max_blocks + page] : -1;
+    int ph = page < a.max_blocks ? a.bt[(int64_t)b * a.max_blocks + page] : -1;
+    if (a.num_blocks > 0 && ph >= a.num_blocks) {
+      if (tok0 < s_len) raise_error(ERR_BAD_PAGE);
+      ph = -1;
+    }
+    s_phys = ph;
   }
   __syncthreads();
   const int L = s_len;
@@ -140,10 +146,10 @@ G9_ERROR_ACCESSORS(gather)
 
 using namespace g9;
 
-extern "C" cudaError_t launch_gather_paged_kv_q8(
+extern "C" cudaError_t gfx906_fa_gather_paged_kv_q8_checked(
     const uint8_t* key_cache_q8, const void* value_cache, const int32_t* block_table,
     const int32_t* seq_lens, uint8_t* k_out, void* v_out, int num_seqs, int num_kv_heads, int Sk,
-    int D, int bytes_per_row, int block_size, int max_blocks_per_seq, int64_t cache_block_stride,
+    int D, int bytes_per_row, int block_size, int max_blocks_per_seq, int num_blocks, int64_t cache_block_stride,
     int64_t cache_token_stride, int64_t cache_head_stride_q8, int64_t v_cache_block_stride,
     int64_t v_cache_token_stride, int64_t v_cache_head_stride, cudaStream_t stream) {
   if (num_seqs == 0 || num_kv_heads == 0 || Sk == 0) return cudaSuccess;
@@ -160,6 +166,7 @@ extern "C" cudaError_t launch_gather_paged_kv_q8(
   a.vc_blk = v_cache_block_stride * 2; a.vc_tok = v_cache_token_stride * 2; a.vc_head = v_cache_head_stride * 2;
   a.B = num_seqs; a.Hkv = num_kv_heads; a.Sk = Sk; a.D = D; a.rb = bytes_per_row;
   a.bs = block_size; a.max_blocks = max_blocks_per_seq;
+  a.num_blocks = num_blocks;
   // K row stores: widest width that keeps every destination row aligned
   const uintptr_t km = (uintptr_t)k_out | (uintptr_t)bytes_per_row | (uintptr_t)key_cache_q8 |
                        (uintptr_t)cache_block_stride | (uintptr_t)cache_token_stride |
@@ -189,4 +196,17 @@ extern "C" cudaError_t launch_gather_paged_kv_q8(
     gather_kernel<false><<<grid, kGatherThreads, 0, stream>>>(a);
   }
   return cudaGetLastError();
+}
+
+extern "C" cudaError_t launch_gather_paged_kv_q8(
+    const uint8_t* key_cache_q8, const void* value_cache, const int32_t* block_table,
+    const int32_t* seq_lens, uint8_t* k_out, void* v_out, int num_seqs, int num_kv_heads, int Sk,
+    int D, int bytes_per_row, int block_size, int max_blocks_per_seq, int64_t cache_block_stride,
+    int64_t cache_token_stride, int64_t cache_head_stride_q8, int64_t v_cache_block_stride,
+    int64_t v_cache_token_stride, int64_t v_cache_head_stride, cudaStream_t stream) {
+  return gfx906_fa_gather_paged_kv_q8_checked(key_cache_q8, value_cache, block_table, seq_lens, k_out, v_out,
+                                              num_seqs, num_kv_heads, Sk, D, bytes_per_row, block_size,
+                                              max_blocks_per_seq, 0, cache_block_stride, cache_token_stride,
+                                              cache_head_stride_q8, v_cache_block_stride, v_cache_token_stride,
+                                              v_cache_head_stride, stream);
 }

@@ -134,10 +134,10 @@ std::vector<torch::Tensor> gather_paged_kv_q8(torch::Tensor key_cache_q8, torch:
   auto k_out = use_or_alloc(k_out_opt, key_cache_q8.options(), rb);
   auto v_out = use_or_alloc(v_out_opt, value_cache.options(), D);
   c10::cuda::CUDAGuard g(key_cache_q8.device());
-  check_status(launch_gather_paged_kv_q8(key_cache_q8.data_ptr<uint8_t>(), value_cache.data_ptr(),
+  check_status(gfx906_fa_gather_paged_kv_q8_checked(key_cache_q8.data_ptr<uint8_t>(), value_cache.data_ptr(),
                                          block_table.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(),
                                          k_out.data_ptr<uint8_t>(), v_out.data_ptr(), B, Hkv, (int)Sk, D,
-                                         rb, bs, MB, (int64_t)bs * Hkv * rb, (int64_t)Hkv * rb, rb,
+                                         rb, bs, MB, NB, (int64_t)bs * Hkv * rb, (int64_t)Hkv * rb, rb,
                                          (int64_t)bs * Hkv * D, (int64_t)Hkv * D, D, cur_stream()),
                "launch_gather_paged_kv_q8");
   return {k_out, v_out};
@@ -230,7 +230,27 @@ G9AttnBatch batch_base(const torch::Tensor& key_cache_q8, const torch::Tensor& v
   b.kv_len = kv_len.data_ptr<int32_t>();
   b.num_seqs = block_table.size(0);
   b.num_heads_kv = key_cache_q8.size(2);
+  b.num_blocks = key_cache_q8.size(0);      // entries past the cache are flagged, never read
   return b;
+}
+
+// Optional score features (not in the reference ops): logit soft-cap,
+// sliding window, per-query-head sinks.  `sinks_c` keeps a contiguous fp32
+// copy alive for the launch.
+void set_features(G9AttnBatch& b, int64_t Hq, double softcap, int64_t window, c10::optional<torch::Tensor>& sinks,
+                  torch::Tensor& sinks_c, const torch::Tensor& like) {
+  TORCH_CHECK(softcap >= 0.0, "softcap must be >= 0 (0 disables it)");
+  TORCH_CHECK(window >= 0, "sliding_window must be >= 0 (0 disables it)");
+  b.softcap = (float)softcap;
+  b.window = (int)window;
+  if (sinks.has_value()) {
+    auto s = sinks.value();
+    CHECK_CUDA(s);
+    TORCH_CHECK(s.dim() == 1 && s.size(0) == Hq, "sinks must be [num_heads_q]");
+    TORCH_CHECK(s.device() == like.device(), "sinks must be on the query's device");
+    sinks_c = s.to(torch::kFloat32).contiguous();
+    b.sinks = sinks_c.data_ptr<float>();
+  }
 }
 
 // 4-D caches hold token rows; a 3-D uint8 [NB, Hkv, record] cache holds
@@ -319,7 +339,8 @@ void set_mask_qabs(G9AttnBatch& b, int64_t B, int64_t Sq, int64_t min_cols, c10:
 // kv_max int32 [B], mask fp16 [B, Sq, >=Skv], q_abs_offset int32 [B].
 torch::Tensor forward(torch::Tensor q, torch::Tensor k_q8, torch::Tensor v, double scale,
                       c10::optional<torch::Tensor> kv_max, c10::optional<torch::Tensor> mask,
-                      c10::optional<torch::Tensor> q_abs_offset) {
+                      c10::optional<torch::Tensor> q_abs_offset, double softcap, int64_t sliding_window,
+                      c10::optional<torch::Tensor> sinks) {
   CHECK_CUDA(q);
   CHECK_CUDA(k_q8);
   CHECK_CUDA(v);
@@ -386,8 +407,9 @@ torch::Tensor forward(torch::Tensor q, torch::Tensor k_q8, torch::Tensor v, doub
   b.num_heads_kv = Hkv;
   b.head_dim = D;
   b.scale = (float)scale;
-  torch::Tensor mask_c, qo_c;
+  torch::Tensor mask_c, qo_c, sinks_c;
   set_mask_qabs(b, B, Sq, Skv, mask, q_abs_offset, mask_c, qo_c);
+  set_features(b, Hq, softcap, sliding_window, sinks, sinks_c, q);
   // contiguous [B, Hkv, Skv, row] tensors are not 16-token pages: the batch
   // goes to the tensor-core path, whose pack step reads any row layout
   run_attention(b, q);
@@ -398,7 +420,8 @@ torch::Tensor forward(torch::Tensor q, torch::Tensor k_q8, torch::Tensor v, doub
 // (fp32 as in the reference; fp16 / bf16 also accepted) -> fp32 [B, Hq, Sq, D].
 torch::Tensor forward_paged_direct(torch::Tensor q, torch::Tensor key_cache_q8, torch::Tensor value_cache,
                                    torch::Tensor block_table, torch::Tensor seq_lens, double scale,
-                                   c10::optional<torch::Tensor> mask, c10::optional<torch::Tensor> q_abs_offset) {
+                                   c10::optional<torch::Tensor> mask, c10::optional<torch::Tensor> q_abs_offset,
+                                   double softcap, int64_t sliding_window, c10::optional<torch::Tensor> sinks) {
   CHECK_CUDA(q);
   CHECK_CONTIG(q);
   TORCH_CHECK(q.dim() == 4, "q must be 4D [B, Hq, Sq, D]");
@@ -427,8 +450,9 @@ torch::Tensor forward_paged_direct(torch::Tensor q, torch::Tensor key_cache_q8, 
   b.num_heads_q = Hq;
   b.head_dim = D;
   b.scale = (float)scale;
-  torch::Tensor mask_c, qo_c;
+  torch::Tensor mask_c, qo_c, sinks_c;
   set_mask_qabs(b, B, Sq, b.max_kv, mask, q_abs_offset, mask_c, qo_c);
+  set_features(b, Hq, softcap, sliding_window, sinks, sinks_c, q);
   run_attention(b, q);
   return out;
 }
@@ -444,7 +468,8 @@ torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, t
                               int64_t max_query_len, int64_t max_seq_len, double scale,
                               c10::optional<torch::Tensor> out_opt,
                               c10::optional<std::vector<int64_t>> query_lens_host,
-                              c10::optional<std::vector<int64_t>> seq_lens_host) {
+                              c10::optional<std::vector<int64_t>> seq_lens_host, double softcap,
+                              int64_t sliding_window, c10::optional<torch::Tensor> sinks) {
   CHECK_CUDA(query);
   CHECK_CUDA(query_start_loc);
   TORCH_CHECK(query.dim() == 3 && query.stride(2) == 1, "query must be [T, Hq, D] with contiguous D");
@@ -468,22 +493,21 @@ torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, t
   }
   if (B == 0 || T == 0) return out;
   c10::cuda::CUDAGuard g(query.device());
-  auto n_q = (query_start_loc.slice(0, 1, B + 1) - query_start_loc.slice(0, 0, B)).to(torch::kInt32);
-  auto q_abs = (seq_lens - n_q).to(torch::kInt32);
   G9AttnBatch b = batch_base(key_cache_q8, value_cache, vfmt, block_table, seq_lens);
   b.q = query.data_ptr();
   b.q_dtype = qdt;
   b.q_tok_stride = query.stride(0);
   b.q_head_stride = query.stride(1);
+  // n_q and the causal offsets (q_abs = seq_len - n_q) are derived in the
+  // kernels from query_start_loc and seq_lens: no extra launches
   b.q_start = query_start_loc.data_ptr<int32_t>();
-  b.n_q = n_q.data_ptr<int32_t>();
+  b.flags = G9_F_CU_SEQLENS | G9_F_CAUSAL_END;
   b.seq_q = (int)max_query_len;
   b.out = out.data_ptr();
   b.out_dtype = dtype_code(out, "out");
   b.o_tok_stride = out.stride(0);
   b.o_head_stride = out.stride(1);
   b.max_kv = (int)max_seq_len;
-  b.q_abs = q_abs.data_ptr<int32_t>();
   b.num_heads_q = Hq;
   b.head_dim = D;
   b.scale = (float)scale;
@@ -496,6 +520,8 @@ torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, t
     TORCH_CHECK((int64_t)seq_lens_host->size() == B, "seq_lens_host must have num_seqs entries");
     for (auto x : *seq_lens_host) kvh.push_back((int)x);
   }
+  torch::Tensor sinks_c;
+  set_features(b, Hq, softcap, sliding_window, sinks, sinks_c, query);
   run_attention(b, query, nqh.empty() ? nullptr : nqh.data(), kvh.empty() ? nullptr : kvh.data());
   return out;
 }
@@ -528,18 +554,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("v_mode") = 1);
   m.def("forward", &forward, "FA forward (Q fp32/fp16/bf16, K q8_0, V fp16): fp32 [B, Hq, Sq, D]",
         py::arg("q"), py::arg("k_q8"), py::arg("v_fp16"), py::arg("scale"), py::arg("kv_max") = c10::nullopt,
-        py::arg("mask") = c10::nullopt, py::arg("q_abs_offset") = c10::nullopt);
+        py::arg("mask") = c10::nullopt, py::arg("q_abs_offset") = c10::nullopt, py::arg("softcap") = 0.0,
+        py::arg("sliding_window") = 0, py::arg("sinks") = c10::nullopt);
   m.def("forward_paged_direct", &forward_paged_direct,
         "Direct-paged flash attention (no gather): q [B, Hq, Sq, D] -> fp32 [B, Hq, Sq, D]",
         py::arg("q"), py::arg("key_cache_q8"), py::arg("value_cache"), py::arg("block_table"),
         py::arg("seq_lens"), py::arg("scale"), py::arg("mask") = c10::nullopt,
-        py::arg("q_abs_offset") = c10::nullopt);
+        py::arg("q_abs_offset") = c10::nullopt, py::arg("softcap") = 0.0, py::arg("sliding_window") = 0,
+        py::arg("sinks") = c10::nullopt);
   m.def("paged_attention", &paged_attention,
         "Varlen causal paged attention in vLLM layout: query [T, Hq, D] -> out [T, Hq, D]",
         py::arg("query"), py::arg("key_cache_q8"), py::arg("value_cache"), py::arg("block_table"),
         py::arg("seq_lens"), py::arg("query_start_loc"), py::arg("max_query_len"), py::arg("max_seq_len"),
         py::arg("scale"), py::arg("out") = c10::nullopt, py::arg("query_lens_host") = c10::nullopt,
-        py::arg("seq_lens_host") = c10::nullopt);
+        py::arg("seq_lens_host") = c10::nullopt, py::arg("softcap") = 0.0, py::arg("sliding_window") = 0,
+        py::arg("sinks") = c10::nullopt);
   m.def("device_error", &device_error, "Read (and optionally clear) the library's device error word",
         py::arg("clear") = false);
 }

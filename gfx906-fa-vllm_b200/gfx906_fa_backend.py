@@ -176,7 +176,7 @@ class Gfx906FABackend(AttentionBackend):
 
     @classmethod
     def supports_sink(cls) -> bool:
-        return False
+        return True
 
     @classmethod
     def supports_attn_type(cls, attn_type: str) -> bool:
@@ -203,12 +203,13 @@ class Gfx906FAImpl(AttentionImpl):
                  use_alibi_sqrt: bool = False) -> None:
         if alibi_slopes is not None:
             raise NotImplementedError("GFX906_FA: alibi_slopes is not supported")
-        if sliding_window is not None:
-            raise NotImplementedError("GFX906_FA: sliding_window is not supported")
-        if logits_soft_cap not in (None, 0, 0.0):
-            raise NotImplementedError("GFX906_FA: logits_soft_cap is not supported")
-        if sinks is not None:
-            raise NotImplementedError("GFX906_FA: sinks are not supported")
+        # Sliding window, logit soft-cap and sinks are computed by the kernels
+        # (the reference rejected all three).  vLLM passes the window as its
+        # size: a query at position p sees keys p - sliding_window + 1 .. p.
+        if sliding_window is not None and sliding_window <= 0:
+            raise ValueError(f"GFX906_FA: sliding_window must be positive, got {sliding_window}")
+        if sinks is not None and tuple(sinks.shape) != (num_heads,):
+            raise ValueError(f"GFX906_FA: sinks must have shape ({num_heads},), got {tuple(sinks.shape)}")
         if attn_type != AttentionType.DECODER:
             raise NotImplementedError(f"GFX906_FA: attn_type={attn_type} is not supported")
         if head_size != 128:
@@ -221,6 +222,9 @@ class Gfx906FAImpl(AttentionImpl):
         self.attn_type = attn_type
         self.kv_sharing_target_layer_name = kv_sharing_target_layer_name
         self.num_queries_per_kv = num_heads // num_kv_heads
+        self.sliding_window = int(sliding_window) if sliding_window else 0
+        self.logits_soft_cap = float(logits_soft_cap) if logits_soft_cap else 0.0
+        self.sinks = sinks
         self._legacy = _os.environ.get("GFX906_FA_LEGACY", "0") == "1"
         self._v_fmt = "q8_0" if _V_FMT in ("q8", "q8_0") else "fp16"
 
@@ -237,6 +241,7 @@ class Gfx906FAImpl(AttentionImpl):
                            kv_cache: torch.Tensor, slot_mapping: torch.Tensor):
         slots = slot_mapping if slot_mapping.dtype == torch.int64 else slot_mapping.to(torch.int64)
         if self._legacy:
+            import vllm._custom_ops  # noqa: F401  (registers torch.ops._C_cache_ops)
             key_cache, value_cache = kv_cache.unbind(1)
             torch.ops._C_cache_ops.reshape_and_cache_flash(
                 key, value, key_cache, value_cache, slots, self.kv_cache_dtype, layer._k_scale, layer._v_scale)
@@ -265,15 +270,26 @@ class Gfx906FAImpl(AttentionImpl):
             key_cache, value_cache = kv_cache.unbind(1)
             res = forward_paged(q, key_cache, value_cache, attn_metadata.block_table, attn_metadata.seq_lens,
                                 attn_metadata.query_start_loc, attn_metadata.max_query_len,
-                                attn_metadata.max_seq_len, scale=self.scale, key_cache_q8=None)
+                                attn_metadata.max_seq_len, scale=self.scale, key_cache_q8=None,
+                                softcap=self.logits_soft_cap, sliding_window=self.sliding_window,
+                                sinks=self._sinks_f32())
             out.copy_(res.view(n, self.num_heads, self.head_size))
             return output
         k_q8, v = kv_cache_views(kv_cache, self._v_fmt)
         forward_paged(q, None, v, attn_metadata.block_table, attn_metadata.seq_lens,
                       attn_metadata.query_start_loc, attn_metadata.max_query_len, attn_metadata.max_seq_len,
                       scale=self.scale, key_cache_q8=k_q8, out=out,
-                      query_lens_host=attn_metadata.query_lens_host, seq_lens_host=attn_metadata.seq_lens_host)
+                      query_lens_host=attn_metadata.query_lens_host, seq_lens_host=attn_metadata.seq_lens_host,
+                      softcap=self.logits_soft_cap, sliding_window=self.sliding_window, sinks=self._sinks_f32())
         return output
+
+    def _sinks_f32(self):
+        """The sinks as fp32 on the layer's device, converted once."""
+        if self.sinks is None:
+            return None
+        if self.sinks.dtype != torch.float32 or not self.sinks.is_contiguous():
+            self.sinks = self.sinks.to(torch.float32).contiguous()
+        return self.sinks
 
 
 # -----------------------------------------------------------------------------

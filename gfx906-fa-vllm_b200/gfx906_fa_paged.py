@@ -133,6 +133,9 @@ def forward_paged(
     out: Optional[torch.Tensor] = None,
     query_lens_host: Optional[list] = None,
     seq_lens_host: Optional[list] = None,
+    softcap: float = 0.0,
+    sliding_window: int = 0,
+    sinks: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """vLLM-layout paged attention (reference: gfx906_fa_paged.py:197-465).
 
@@ -141,7 +144,12 @@ def forward_paged(
     result is written there directly and `out` is returned.  Causal with
     q_abs = seq_len - n_q when max_seqlen_q > 1 (gfx906_fa_paged.py:289-295);
     decode rows see their whole context.  q_pad_buf / mask_buf are accepted
-    for signature compatibility and unused (no padding is needed)."""
+    for signature compatibility and unused (no padding is needed).
+
+    Beyond the reference: `softcap` (> 0: score -> softcap * tanh(score /
+    softcap)), `sliding_window` (> 0: a query at position qp sees keys k with
+    qp - k < sliding_window) and `sinks` ([Hq] logits added to each softmax
+    denominator), on every path."""
     num_tokens, Hq, D = query.shape
     num_seqs = block_table.shape[0]
     if scale is None:
@@ -162,7 +170,8 @@ def forward_paged(
                                                     device=query.device)
         gfx906_fa.paged_attention(query, key_cache_q8, value_cache, bt, sl, cu, int(max_seqlen_q),
                                   int(max_seqlen_k), float(scale), out=o, query_lens_host=query_lens_host,
-                                  seq_lens_host=seq_lens_host)
+                                  seq_lens_host=seq_lens_host, softcap=float(softcap),
+                                  sliding_window=int(sliding_window), sinks=sinks)
         return o if out is not None else o.view(num_tokens, Hq * D)
 
     # ---- gather + flat forward (reference fused / legacy paths) -------------
@@ -191,7 +200,8 @@ def forward_paged(
     q_padded = torch.zeros((num_seqs, Hq, max_seqlen_q, D), dtype=query.dtype, device=query.device)
     q_padded[seq_of_tok, :, pos_in_seq] = query
     q_abs = (sl.to(torch.long) - n_q).to(torch.int32) if max_seqlen_q > 1 else None
-    o_pad = gfx906_fa.forward(q_padded, K_q8, V, float(scale), kv_max=sl, q_abs_offset=q_abs)
+    o_pad = gfx906_fa.forward(q_padded, K_q8, V, float(scale), kv_max=sl, q_abs_offset=q_abs,
+                              softcap=float(softcap), sliding_window=int(sliding_window), sinks=sinks)
     o_flat = o_pad[seq_of_tok, :, pos_in_seq]                     # [T, Hq, D] fp32
     if out is not None:
         out.copy_(o_flat)

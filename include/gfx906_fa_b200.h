@@ -76,6 +76,18 @@ cudaError_t launch_gather_paged_kv_q8(const uint8_t* key_cache_q8, const void* v
 /* New entry points                                                         */
 /* ======================================================================= */
 
+/* launch_gather_paged_kv_q8 with the cache's page count: block-table entries
+ * >= num_blocks are treated like negative ones (the page counts as out of
+ * range) and set bit 1 of the device error word, so a corrupt table cannot
+ * send a copy outside the cache allocation.  num_blocks <= 0 checks nothing
+ * (the reference launcher's behaviour). */
+cudaError_t gfx906_fa_gather_paged_kv_q8_checked(
+    const uint8_t* key_cache_q8, const void* value_cache, const int32_t* block_table, const int32_t* seq_lens,
+    uint8_t* k_out, void* v_out, int num_seqs, int num_kv_heads, int Sk, int D, int bytes_per_row, int block_size,
+    int max_blocks_per_seq, int num_blocks, int64_t cache_block_stride, int64_t cache_token_stride,
+    int64_t cache_head_stride_q8, int64_t v_cache_block_stride, int64_t v_cache_token_stride,
+    int64_t v_cache_head_stride, cudaStream_t stream);
+
 /* Dense Q8_0 quantisation of N rows of D elements of type x_dtype
  * (G9_DT_*) -- the dtype-generic form of launch_quantize_q8_0_dense. */
 cudaError_t gfx906_fa_quantize_q8_0(const void* x, int x_dtype, uint8_t* y, int64_t N, int D,
@@ -139,7 +151,19 @@ cudaError_t gfx906_fa_store_kv(const void* key, int key_dtype, int64_t key_token
  * mask[b*mask_seq_stride + t*mask_tok_stride + k] to the scaled score
  * (kernel/fattn-q8.cuh:628-631).  Query heads map to kv heads by
  * hq / (num_heads_q / num_heads_kv).  A query row with no visible key is
- * written as zeros. */
+ * written as zeros.
+ *
+ * Query positions: token t of sequence b sits at qp = q_abs[b] + t, or at
+ * kv_len[b] - n_q[b] + t without q_abs (the last query token is the last
+ * key).  The sliding window keeps keys qp - window < k <= (causal limit);
+ * the reference kernel's logit soft-cap (kernel/fattn-q8.cuh:638-640) maps
+ * the scaled score s to softcap * tanh(s / softcap) before the mask is added;
+ * a sink adds exp(sink[hq]) (relative to the row's max) to the softmax
+ * denominator of every row of query head hq, as vLLM's attention-sink models
+ * define it.  kv_len[b] is clamped to max_blocks * block_size and to max_kv.
+ * A block-table entry that is negative, or >= num_blocks when num_blocks > 0,
+ * is never dereferenced: it sets bit 1 of the device error word and its keys
+ * are dropped (decode) or read as zero vectors (prefill). */
 typedef struct G9AttnBatch {
   const void* q;
   int q_dtype;
@@ -165,7 +189,20 @@ typedef struct G9AttnBatch {
   int64_t mask_seq_stride, mask_tok_stride;
   int num_seqs, num_heads_q, num_heads_kv, head_dim;
   float scale;
+  /* Fields below are optional; a zero-initialised value turns each off. */
+  int num_blocks;       /* pages in the cache: entries >= num_blocks (and < 0) are bad pages (0: not checked) */
+  float softcap;        /* > 0: scaled score s -> softcap * tanh(s / softcap), before the mask */
+  int window;           /* > 0: sliding window, key k visible to query position qp only if qp - k < window */
+  const float* sinks;   /* [num_heads_q] fp32 logits (scaled-score units) added to each row's softmax
+                           denominator only, or NULL */
+  int flags;            /* G9_F_* below */
 } G9AttnBatch;
+
+/* G9AttnBatch.flags */
+#define G9_F_CU_SEQLENS 1  /* n_q == NULL: q_start holds num_seqs + 1 offsets (vLLM's query_start_loc) and
+                              n_q[b] = q_start[b + 1] - q_start[b] */
+#define G9_F_CAUSAL_END 2  /* q_abs == NULL: causal with q_abs[b] = kv_len[b] - n_q[b] (the query chunk
+                              ends at the last key, vLLM's chunked-prefill convention) */
 
 /* Split-K flash decoding straight from the paged Q8 cache (no gather):
  * persistent CTAs walk (KV chunk, kv-head group, sequence) items, stream
@@ -265,6 +302,14 @@ cudaError_t gfx906_fa_launch_paged(const float* Q_fp32, const void* K_paged, con
  * gfx906_fa_clear_device_error resets it to zero. */
 cudaError_t gfx906_fa_get_device_error(unsigned int* out);
 cudaError_t gfx906_fa_clear_device_error(void);
+
+/* Self-test of the bounded waits every kernel uses: launches one thread that
+ * waits on an mbarrier nothing arrives at, with a limit of limit_ns
+ * (<= 100 ms).  The wait gives up, sets bit 0 of the device error word and
+ * writes 1 to *done (device int; 2 would mean the wait completed).  The
+ * context stays usable.  No reference counterpart (failure-detection test
+ * hook). */
+cudaError_t gfx906_fa_selftest_wait_timeout(uint64_t limit_ns, int* done, cudaStream_t stream);
 
 /* Library version string (static storage). */
 const char* gfx906_fa_version(void);

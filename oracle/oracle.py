@@ -183,7 +183,9 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
                     o_strides: tuple[int, int, int] | None = None,
                     k_strides: tuple[int, int, int] | None = None,
                     v_strides: tuple[int, int, int] | None = None,
-                    nthreads: int = 0, bs: int | None = None, v_fmt: str | None = None) -> np.ndarray:
+                    nthreads: int = 0, bs: int | None = None, v_fmt: str | None = None,
+                    softcap: float = 0.0, window: int = 0, sinks: np.ndarray | None = None,
+                    num_blocks: int = 0) -> np.ndarray:
     """fp32 dequant + softmax reference (double accumulation).
 
     Default layouts are vLLM's: q [T, Hq, D] with token rows q_start[b] + t;
@@ -193,6 +195,11 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
     k_cache.shape[1]); v_fmt: "f16" (default), "bf16", "q8" (= v_q8) or "q8t"
     (page-transposed Q8_0 records, v_cache [NB, Hkv, bs*D/32*34], v_strides
     (page, unused, head)).
+    softcap > 0: score s -> softcap * tanh(s / softcap) before the mask;
+    window > 0: key k visible to query position qp only if qp - k < window
+    (qp = q_abs + t, or kv_len - n_q + t without q_abs); sinks [Hq] fp32:
+    exp(sink) joins each row's softmax denominator; num_blocks > 0: keys on
+    pages whose entry is < 0 or >= num_blocks are dropped.
     """
     vcode = {"f16": 0, "bf16": 1, "q8": 2, "q8t": 3}[v_fmt or ("q8" if v_q8 else "f16")]
     v_q8 = vcode == 2
@@ -226,7 +233,8 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
     if mask is not None:
         mk = np.ascontiguousarray(mask).view(np.uint16)
         m_seq, m_tok = mk.shape[1] * mk.shape[2], mk.shape[2]
-    lib().q8o_attention(
+    sk = None if sinks is None else np.ascontiguousarray(sinks, dtype=np.float32)
+    lib().q8o_attention_ex(
         _p(q.view(np.uint16) if q.dtype != np.float32 else q), ctypes.c_int(_dtype_code(q, q_dtype)),
         _i64(q_strides[0]), _i64(q_strides[1]), _i64(q_strides[2]), _p(qs), _p(nq),
         _p(out), _i64(o_strides[0]), _i64(o_strides[1]), _i64(o_strides[2]),
@@ -235,7 +243,8 @@ def attention_paged(q: np.ndarray, q_dtype: str | None, q_start: np.ndarray, n_q
         _i64(v_strides[0]), _i64(v_strides[1]), _i64(v_strides[2]), _p(bt), ctypes.c_int(max_blocks),
         ctypes.c_int(bs), _p(kl), _p(qa), _p(mk), _i64(m_seq), _i64(m_tok), ctypes.c_int(B),
         ctypes.c_int(Hq), ctypes.c_int(Hkv), ctypes.c_int(D), ctypes.c_float(scale),
-        ctypes.c_int(nthreads))
+        ctypes.c_int(nthreads), ctypes.c_float(softcap), ctypes.c_int(int(window)), _p(sk),
+        ctypes.c_int(int(num_blocks)))
     return out
 
 

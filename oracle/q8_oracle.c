@@ -27,6 +27,19 @@
  *                          additive fp16 mask of kernel/fattn-q8.cuh:628-631,
  *                          the KV_max cut-off of kernel/fattn-q8.cuh:946, and
  *                          softmax + P.V accumulated in double.
+ *   q8o_attention_ex       the same with the optional score features:
+ *                          the logit soft-cap of kernel/fattn-q8.cuh:638-640
+ *                          (softcap * tanh(s / softcap) on the scaled score,
+ *                          before the mask); a sliding window and per-head
+ *                          sinks as vLLM's attention interface defines them
+ *                          (the reference backend rejects both,
+ *                          extension/gfx906_fa_backend.py:249-254): key k is
+ *                          visible to query position qp iff qp - k < window,
+ *                          qp = q_abs + t (or kv_len - n_q + t without
+ *                          q_abs), and exp(sink[hq]) joins the softmax
+ *                          denominator only.  num_blocks > 0: keys on pages
+ *                          whose block-table entry is negative or
+ *                          >= num_blocks are dropped.
  *
  * The only fp16 arithmetic needed is float <-> binary16 conversion, written
  * here from the IEEE-754 definition (round to nearest, ties to even).
@@ -259,16 +272,16 @@ void q8o_dequant_q8t(const uint8_t* rec, int D, int bs, int t, float* out) {
  *   mask     optional fp16 additive bias, mask[b*mask_seq_stride + t*mask_tok_stride + k]
  * Rows with no visible key are written as zeros.
  */
-void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_tok_stride,
-                   int64_t q_head_stride, const int32_t* q_start, const int32_t* n_q,
-                   float* out, int64_t o_seq_stride, int64_t o_tok_stride, int64_t o_head_stride,
-                   const uint8_t* k_cache, const uint8_t* v_cache, int v_fmt,
-                   int64_t k_page_stride, int64_t k_tok_stride, int64_t k_head_stride,
-                   int64_t v_page_stride, int64_t v_tok_stride, int64_t v_head_stride,
-                   const int32_t* block_table, int max_blocks, int bs, const int32_t* kv_len,
-                   const int32_t* q_abs, const uint16_t* mask, int64_t mask_seq_stride,
-                   int64_t mask_tok_stride, int B, int Hq, int Hkv, int D, float scale,
-                   int nthreads) {
+void q8o_attention_ex(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_tok_stride,
+                      int64_t q_head_stride, const int32_t* q_start, const int32_t* n_q,
+                      float* out, int64_t o_seq_stride, int64_t o_tok_stride, int64_t o_head_stride,
+                      const uint8_t* k_cache, const uint8_t* v_cache, int v_fmt,
+                      int64_t k_page_stride, int64_t k_tok_stride, int64_t k_head_stride,
+                      int64_t v_page_stride, int64_t v_tok_stride, int64_t v_head_stride,
+                      const int32_t* block_table, int max_blocks, int bs, const int32_t* kv_len,
+                      const int32_t* q_abs, const uint16_t* mask, int64_t mask_seq_stride,
+                      int64_t mask_tok_stride, int B, int Hq, int Hkv, int D, float scale,
+                      int nthreads, float softcap, int window, const float* sinks, int num_blocks) {
     const int G = Hq / Hkv;
     /* flatten (b, hq, t) work items */
     int64_t total = 0;
@@ -308,13 +321,24 @@ void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_t
             const int64_t qoff = b * q_seq_stride + ((int64_t)q_start[b] + t) * q_tok_stride + hq * q_head_stride;
             for (int d = 0; d < D; ++d) qrow[d] = load_elem(q, qoff + d, q_dtype);
             double m = -INFINITY;
+            int kmin = 0;
+            if (window > 0) {
+                const int64_t qp = (q_abs ? (int64_t)q_abs[b] : (int64_t)L - n_q[b]) + t;
+                const int64_t lo = qp - window + 1;
+                kmin = lo < 0 ? 0 : (lo > kmax ? kmax : (int)lo);
+            }
             for (int k = 0; k < kmax; ++k) {
                 const int phys = block_table[(int64_t)b * max_blocks + k / bs];
+                if (k < kmin || (num_blocks > 0 && (phys < 0 || phys >= num_blocks))) {
+                    sc[k] = -INFINITY;
+                    continue;
+                }
                 const uint8_t* kr = k_cache + phys * k_page_stride + (k % bs) * k_tok_stride + h * k_head_stride;
                 q8o_dequant_row(kr, D, krow);
                 double s = 0.0;
                 for (int d = 0; d < D; ++d) s += (double)qrow[d] * (double)krow[d];
                 s *= (double)scale;
+                if (softcap > 0.0f) s = (double)softcap * tanh(s / (double)softcap);
                 if (mask) s += (double)q8o_f16_to_f32(mask[b * mask_seq_stride + (int64_t)t * mask_tok_stride + k]);
                 sc[k] = s;
                 if (s > m) m = s;
@@ -322,6 +346,7 @@ void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_t
             for (int d = 0; d < D; ++d) acc[d] = 0.0;
             double l = 0.0;
             if (m == -INFINITY) { for (int d = 0; d < D; ++d) o[d] = 0.0f; continue; }
+            if (sinks) l += exp((double)sinks[hq] - m);
             for (int k = 0; k < kmax; ++k) {
                 const double p = exp(sc[k] - m);
                 if (p == 0.0) continue;
@@ -343,4 +368,21 @@ void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_t
         }
         free(sc);
     }
+}
+
+void q8o_attention(const void* q, int q_dtype, int64_t q_seq_stride, int64_t q_tok_stride,
+                   int64_t q_head_stride, const int32_t* q_start, const int32_t* n_q,
+                   float* out, int64_t o_seq_stride, int64_t o_tok_stride, int64_t o_head_stride,
+                   const uint8_t* k_cache, const uint8_t* v_cache, int v_fmt,
+                   int64_t k_page_stride, int64_t k_tok_stride, int64_t k_head_stride,
+                   int64_t v_page_stride, int64_t v_tok_stride, int64_t v_head_stride,
+                   const int32_t* block_table, int max_blocks, int bs, const int32_t* kv_len,
+                   const int32_t* q_abs, const uint16_t* mask, int64_t mask_seq_stride,
+                   int64_t mask_tok_stride, int B, int Hq, int Hkv, int D, float scale,
+                   int nthreads) {
+    q8o_attention_ex(q, q_dtype, q_seq_stride, q_tok_stride, q_head_stride, q_start, n_q, out, o_seq_stride,
+                     o_tok_stride, o_head_stride, k_cache, v_cache, v_fmt, k_page_stride, k_tok_stride,
+                     k_head_stride, v_page_stride, v_tok_stride, v_head_stride, block_table, max_blocks, bs,
+                     kv_len, q_abs, mask, mask_seq_stride, mask_tok_stride, B, Hq, Hkv, D, scale, nthreads,
+                     0.0f, 0, 0, 0);
 }

@@ -71,8 +71,9 @@ class PagedCase:
         vb = self.rb if self.v_fmt == "q8" else 2 * self.D
         return (self.bs * self.Hkv * vb, self.Hkv * vb, vb)
 
-    def oracle_varlen(self, q, q_dtype, n_q, causal=True, q_abs=None, mask=None, pick=None):
-        """q [T, Hq, D] numpy (fp16 / fp32 / bf16-as-uint16)."""
+    def oracle_varlen(self, q, q_dtype, n_q, causal=True, q_abs=None, mask=None, pick=None, **feat):
+        """q [T, Hq, D] numpy (fp16 / fp32 / bf16-as-uint16).  `feat`:
+        softcap / window / sinks / num_blocks of oracle.attention_paged."""
         n_q = np.asarray(n_q, np.int32)
         q_start = np.concatenate([[0], np.cumsum(n_q)[:-1]]).astype(np.int32)
         if causal and q_abs is None:
@@ -80,9 +81,22 @@ class PagedCase:
         return O.attention_paged(q, q_dtype, q_start, n_q, self.k_np, self.v_np,
                                  self.block_table.numpy(), self.seq_lens, self.scale, self.Hkv,
                                  q_abs=q_abs if causal else None, mask=mask, v_fmt=self.v_fmt,
-                                 v_strides=self._v_strides())
+                                 v_strides=self._v_strides(), **feat)
 
-    def oracle_bhsd(self, q, q_dtype, q_abs=None, mask=None, pick=None):
+    def oracle_rows(self, q_rows, q_dtype, seq, q_abs_rows, **feat):
+        """Selected query tokens only: q_rows [n, Hq, D] are single tokens of
+        sequences seq[i] at causal positions q_abs_rows[i] (the token sees
+        keys <= q_abs_rows[i]).  Each becomes a one-token pseudo-sequence
+        over its sequence's block-table row, so long contexts stay cheap."""
+        seq = np.asarray(seq, np.int64)
+        n = len(seq)
+        bt = self.block_table.numpy()[seq]
+        return O.attention_paged(np.ascontiguousarray(q_rows), q_dtype, np.arange(n, dtype=np.int32),
+                                 np.ones(n, np.int32), self.k_np, self.v_np, bt, self.seq_lens[seq], self.scale,
+                                 self.Hkv, q_abs=np.asarray(q_abs_rows, np.int32), v_fmt=self.v_fmt,
+                                 v_strides=self._v_strides(), **feat)
+
+    def oracle_bhsd(self, q, q_dtype, q_abs=None, mask=None, pick=None, **feat):
         """q [B', Hq, Sq, D] padded layout (forward_paged_direct); `pick`
         selects which sequences q belongs to (default: all)."""
         B, Hq, Sq, D = q.shape
@@ -92,7 +106,7 @@ class PagedCase:
                                  self.k_np, self.v_np, bt, sl, self.scale, self.Hkv, q_abs=q_abs, mask=mask,
                                  v_fmt=self.v_fmt, q_strides=(Hq * Sq * D, D, Sq * D),
                                  out_shape=(B, Hq, Sq, D), o_strides=(Hq * Sq * D, D, Sq * D),
-                                 v_strides=self._v_strides())
+                                 v_strides=self._v_strides(), **feat)
 
 
 def assert_close(out, ref, atol=ATOL, rtol=RTOL, what=""):

@@ -19,6 +19,29 @@ def header_functions(path=HEADER):
                       src, flags=re.M)
 
 
+class G9AttnBatch(ctypes.Structure):
+    """ctypes mirror of G9AttnBatch (include/gfx906_fa_b200.h), field for field."""
+    _fields_ = [
+        ("q", ctypes.c_void_p), ("q_dtype", ctypes.c_int),
+        ("q_seq_stride", ctypes.c_int64), ("q_tok_stride", ctypes.c_int64), ("q_head_stride", ctypes.c_int64),
+        ("q_start", ctypes.c_void_p), ("n_q", ctypes.c_void_p), ("seq_q", ctypes.c_int),
+        ("out", ctypes.c_void_p), ("out_dtype", ctypes.c_int),
+        ("o_seq_stride", ctypes.c_int64), ("o_tok_stride", ctypes.c_int64), ("o_head_stride", ctypes.c_int64),
+        ("k_cache", ctypes.c_void_p),
+        ("k_page_stride", ctypes.c_int64), ("k_tok_stride", ctypes.c_int64), ("k_head_stride", ctypes.c_int64),
+        ("v_cache", ctypes.c_void_p),
+        ("v_page_stride", ctypes.c_int64), ("v_tok_stride", ctypes.c_int64), ("v_head_stride", ctypes.c_int64),
+        ("v_fmt", ctypes.c_int), ("block_table", ctypes.c_void_p), ("max_blocks", ctypes.c_int),
+        ("block_size", ctypes.c_int), ("kv_len", ctypes.c_void_p), ("max_kv", ctypes.c_int),
+        ("q_abs", ctypes.c_void_p), ("mask", ctypes.c_void_p),
+        ("mask_seq_stride", ctypes.c_int64), ("mask_tok_stride", ctypes.c_int64),
+        ("num_seqs", ctypes.c_int), ("num_heads_q", ctypes.c_int), ("num_heads_kv", ctypes.c_int),
+        ("head_dim", ctypes.c_int), ("scale", ctypes.c_float),
+        ("num_blocks", ctypes.c_int), ("softcap", ctypes.c_float), ("window", ctypes.c_int),
+        ("sinks", ctypes.c_void_p), ("flags", ctypes.c_int),
+    ]
+
+
 def capi():
     return ctypes.CDLL(LIB)
 

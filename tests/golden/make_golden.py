@@ -149,8 +149,11 @@ def make_config1(paged, tq, trt, tic, out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("GFX906_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("GFX906_REFERENCE"),
+                    help="checkout of the reference project (or set $GFX906_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or $GFX906_REFERENCE) is required")
     torch.set_num_threads(4)
     paged, tq, trt, tg, tic = _import_reference(args.reference)
     quant, gath, cfg1 = {}, {}, {}

@@ -47,9 +47,27 @@ def test_impl_rejects_unsupported_features():
     kw = dict(num_heads=8, head_size=128, scale=0.1, num_kv_heads=2, alibi_slopes=None,
               sliding_window=None, kv_cache_dtype="auto")
     be.Gfx906FAImpl(**kw)
-    for bad in (dict(alibi_slopes=[1.0] * 8), dict(sliding_window=128), dict(logits_soft_cap=30.0)):
+    for bad in (dict(alibi_slopes=[1.0] * 8), dict(head_size=64)):
         with pytest.raises(NotImplementedError):
             be.Gfx906FAImpl(**{**kw, **bad})
+    # malformed feature arguments are rejected, not ignored
+    import torch
+    for bad in (dict(sliding_window=-4), dict(sinks=torch.zeros(3))):
+        with pytest.raises(ValueError):
+            be.Gfx906FAImpl(**{**kw, **bad})
+
+
+def test_impl_accepts_window_softcap_sinks():
+    """Sliding window, logit soft-cap and sinks are computed by the kernels
+    (the reference backend rejected them, extension/gfx906_fa_backend.py:249-254)."""
+    be = _backend()
+    import torch
+    impl = be.Gfx906FAImpl(num_heads=8, head_size=128, scale=0.1, num_kv_heads=2, alibi_slopes=None,
+                           sliding_window=4096, kv_cache_dtype="auto", logits_soft_cap=30.0,
+                           sinks=torch.zeros(8, dtype=torch.bfloat16))
+    assert impl.sliding_window == 4096 and impl.logits_soft_cap == 30.0
+    assert impl._sinks_f32().dtype == torch.float32
+    assert be.Gfx906FABackend.supports_sink()
 
 
 def test_kv_cache_views_layout():

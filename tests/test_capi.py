@@ -64,7 +64,7 @@ def test_decode_plans_dense_pages_for_every_head_count(hkv, v_fmt):
     parallel rank can hold (a rejection would silently route decode to the
     128-row tensor-core prefill kernel).  v_fmt 0: fp16 V rows; 3: page-
     transposed Q8_0 V records."""
-    from test_zz_no_alloc import G9AttnBatch
+    from _util import G9AttnBatch
     lib = capi()
     lib.gfx906_fa_decode_workspace_size.restype = ctypes.c_size_t
     lib.gfx906_fa_decode_workspace_size.argtypes = [ctypes.POINTER(G9AttnBatch)]
@@ -88,3 +88,24 @@ def test_decode_plans_dense_pages_for_every_head_count(hkv, v_fmt):
     b.num_seqs, b.num_heads_q, b.num_heads_kv, b.head_dim = B, 6 * hkv, hkv, D
     b.scale = 0.088
     assert lib.gfx906_fa_decode_workspace_size(ctypes.byref(b)) > 0
+
+
+def test_ctypes_batch_matches_c_layout(tmp_path):
+    """The tests' ctypes G9AttnBatch has the C struct's size and field
+    offsets (compiled with gcc against include/gfx906_fa_b200.h)."""
+    import shutil
+    import subprocess
+    from _util import G9AttnBatch
+    if not shutil.which("gcc") or not os.path.exists("/usr/local/cuda/include/cuda_runtime_api.h"):
+        pytest.skip("gcc / CUDA headers not available")
+    names = [f[0] for f in G9AttnBatch._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "gfx906_fa_b200.h"\nint main(void) {\n'
+                   '  printf("%zu\\n", sizeof(G9AttnBatch));\n' +
+                   "".join(f'  printf("%zu\\n", offsetof(G9AttnBatch, {n}));\n' for n in names) + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.check_call(["gcc", "-I", os.path.join(ROOT, "include"), "-I", "/usr/local/cuda/include",
+                           str(src), "-o", str(exe)])
+    vals = [int(x) for x in subprocess.check_output([str(exe)]).split()]
+    assert vals[0] == ctypes.sizeof(G9AttnBatch)
+    assert vals[1:] == [getattr(G9AttnBatch, n).offset for n in names]

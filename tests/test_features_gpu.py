@@ -1,0 +1,170 @@
+"""Logit soft-cap, sliding window and attention sinks in the decode and
+prefill kernels, against the fp32 oracle (|d| <= 2e-3 + 1e-2 |ref|).
+
+The reference kernel carries the soft-cap (kernel/fattn-q8.cuh:638-640) and
+its backend rejects all three features (extension/gfx906_fa_backend.py:
+249-254); the window and sinks follow vLLM's attention interface (a query at
+position p sees keys p - window + 1 .. p; exp(sink) joins the softmax
+denominator)."""
+import numpy as np
+import pytest
+import torch
+
+from _paged import PagedCase, assert_close
+from _util import to_np
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def _gfx():
+    import gfx906_fa
+    return gfx906_fa
+
+
+def _q(shape, dtype, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype)
+
+
+def _cu(nq):
+    return torch.tensor(np.concatenate([[0], np.cumsum(nq)]), dtype=torch.int32)
+
+
+def _sinks(Hq, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn((Hq,), generator=g) * 2.0
+
+
+FEATS = {
+    "softcap": dict(softcap=4.0),
+    "window": dict(window=700),
+    "sinks": dict(sinks=True),
+    "all": dict(softcap=6.0, window=333, sinks=True),
+}
+
+
+def _run_varlen(case, q, nq, lens, feat, Hq, host=True):
+    sinks = _sinks(Hq, 5) if feat.get("sinks") else None
+    kw = dict(softcap=feat.get("softcap", 0.0), sliding_window=feat.get("window", 0),
+              sinks=None if sinks is None else sinks.to(dev))
+    if host:
+        kw.update(query_lens_host=nq, seq_lens_host=lens)
+    out = _gfx().paged_attention(q.to(dev), case.k_cache, case.v_cache, case.block_table.to(dev),
+                                 torch.from_numpy(case.seq_lens).to(dev), _cu(nq).to(dev), max(nq), max(lens),
+                                 case.scale, **kw)
+    ofeat = dict(softcap=feat.get("softcap", 0.0), window=feat.get("window", 0),
+                 sinks=None if sinks is None else sinks.numpy())
+    return to_np(out.float()), ofeat
+
+
+@pytest.mark.parametrize("v_fmt", ["q8t", "f16", "q8"])
+@pytest.mark.parametrize("name", list(FEATS))
+def test_decode_features(v_fmt, name):
+    """Decode batch (transposed consumer for q8t / f16 V, 16-row consumer for
+    Q8_0 V rows) with 4-token verify rows and long contexts, so the window
+    skips whole pages and the split-K combine adds the sinks."""
+    lens, nq = [3000, 700, 37, 15000, 9000], [1, 1, 1, 4, 1]
+    case = PagedCase(lens, 8, v_fmt=v_fmt, seed=11)
+    q = _q((sum(nq), 48, 128), torch.bfloat16, seed=12, scale=3.0)   # scores large enough to cap
+    out, ofeat = _run_varlen(case, q, nq, lens, FEATS[name], 48)
+    ref = case.oracle_varlen(to_np(q), "bf16", nq, **ofeat)
+    assert_close(out, ref, what=f"decode {name} ({v_fmt} V)")
+    assert _gfx().device_error(True) == 0
+
+
+@pytest.mark.parametrize("name", list(FEATS))
+def test_decode_features_many_rows(name):
+    """5 query tokens x GQA 6 = 30 rows: the two-m-tile 16-row consumer."""
+    lens, nq = [4000, 1200], [5, 5]
+    case = PagedCase(lens, 8, v_fmt="q8t", seed=13)
+    q = _q((sum(nq), 48, 128), torch.float16, seed=14, scale=3.0)
+    out, ofeat = _run_varlen(case, q, nq, lens, FEATS[name], 48)
+    assert_close(out, case.oracle_varlen(to_np(q), None, nq, **ofeat), what=f"decode 30 rows {name}")
+
+
+@pytest.mark.parametrize("Hkv", [1, 2, 4])
+def test_decode_features_small_head_counts(Hkv):
+    """Per-GPU shapes of tensor parallelism (1, 2, 4 kv heads)."""
+    lens, nq = [5000, 800, 12000], [1, 1, 1]
+    Hq = 6 * Hkv
+    case = PagedCase(lens, Hkv, v_fmt="q8t", seed=15 + Hkv)
+    q = _q((sum(nq), Hq, 128), torch.bfloat16, seed=16, scale=3.0)
+    out, ofeat = _run_varlen(case, q, nq, lens, FEATS["all"], Hq)
+    assert_close(out, case.oracle_varlen(to_np(q), "bf16", nq, **ofeat), what=f"decode all Hkv={Hkv}")
+
+
+@pytest.mark.parametrize("v_fmt", ["q8t", "f16"])
+@pytest.mark.parametrize("name", list(FEATS))
+def test_prefill_features(v_fmt, name):
+    """Chunked prefill on the tensor cores: a 700-token chunk at offset
+    1300 (window tiles skipped before the first row's window) and a full
+    causal 400-token prefill in one batch."""
+    lens, nq = [2000, 400], [700, 400]
+    case = PagedCase(lens, 8, v_fmt=v_fmt, seed=21)
+    q = _q((sum(nq), 48, 128), torch.float16, seed=22, scale=3.0)
+    out, ofeat = _run_varlen(case, q, nq, lens, FEATS[name], 48)
+    ref = case.oracle_varlen(to_np(q), None, nq, **ofeat)
+    assert_close(out, ref, what=f"prefill {name} ({v_fmt} V)")
+    assert _gfx().device_error(True) == 0
+
+
+def test_mixed_batch_features_without_host_lengths():
+    """No host lengths: both kernels pick their sequences on the device."""
+    lens, nq = [900, 64, 3000], [300, 1, 4]
+    case = PagedCase(lens, 8, v_fmt="q8t", seed=23)
+    q = _q((sum(nq), 48, 128), torch.bfloat16, seed=24, scale=3.0)
+    out, ofeat = _run_varlen(case, q, nq, lens, FEATS["all"], 48, host=False)
+    assert_close(out, case.oracle_varlen(to_np(q), "bf16", nq, **ofeat), what="mixed all")
+
+
+def test_direct_paged_window_without_causal_offsets():
+    """forward_paged_direct without q_abs: the last query token sits at the
+    last key, so a decode token's window is the last `window` keys."""
+    lens = [1500, 37, 700]
+    case = PagedCase(lens, 8, seed=25)
+    q = _q((3, 48, 1, 128), torch.float32, seed=26, scale=3.0)
+    sinks = _sinks(48, 27)
+    out = _gfx().forward_paged_direct(q.to(dev), case.k_cache, case.v_cache, case.block_table.to(dev),
+                                      torch.from_numpy(case.seq_lens).to(dev), case.scale, softcap=5.0,
+                                      sliding_window=256, sinks=sinks.to(dev))
+    ref = case.oracle_bhsd(to_np(q), None, softcap=5.0, window=256, sinks=sinks.numpy())
+    assert_close(to_np(out), ref, what="direct window")
+
+
+def test_flat_forward_features():
+    """The flat `forward` op (gather path) with window, soft-cap and sinks."""
+    import oracle as O
+    g = _gfx()
+    B, Hq, Hkv, D, Sq, Skv = 2, 8, 2, 128, 200, 640
+    k = _q((B, Hkv, Skv, D), torch.float16, seed=1)
+    v = _q((B, Hkv, Skv, D), torch.float16, seed=2)
+    q = _q((B, Hq, Sq, D), torch.float32, seed=3, scale=3.0)
+    k_q8 = g.quantize_q8_0(k.to(dev))
+    qa = torch.tensor([Skv - Sq, 100], dtype=torch.int32)
+    sinks = _sinks(Hq, 4)
+    out = g.forward(q.to(dev), k_q8, v.to(dev), 1.0 / np.sqrt(D), q_abs_offset=qa.to(dev), softcap=5.0,
+                    sliding_window=150, sinks=sinks.to(dev))
+    # oracle over the same contiguous layout (one page of Skv tokens per sequence)
+    rb = 136
+    ref = O.attention_paged(to_np(q), None, np.zeros(B, np.int32), np.full(B, Sq, np.int32), to_np(k_q8),
+                            to_np(v), np.arange(B, dtype=np.int32).reshape(B, 1), np.full(B, Skv, np.int32),
+                            1.0 / np.sqrt(D), Hkv, q_abs=to_np(qa), q_strides=(Hq * Sq * D, D, Sq * D),
+                            out_shape=(B, Hq, Sq, D), o_strides=(Hq * Sq * D, D, Sq * D),
+                            k_strides=(Hkv * Skv * rb, rb, Skv * rb), v_strides=(Hkv * Skv * 256, 256, Skv * 256),
+                            bs=Skv, softcap=5.0, window=150, sinks=sinks.numpy())
+    assert_close(to_np(out), ref, what="flat forward features")
+
+
+def test_features_off_is_bitwise_default():
+    """softcap=0, sliding_window=0, sinks=None take the default kernels:
+    bitwise the same output as a call without the arguments."""
+    lens, nq = [3000, 700], [1, 1]
+    case = PagedCase(lens, 8, v_fmt="q8t", seed=28)
+    q = _q((2, 48, 128), torch.bfloat16, seed=29)
+    g = _gfx()
+    args = (q.to(dev), case.k_cache, case.v_cache, case.block_table.to(dev),
+            torch.from_numpy(case.seq_lens).to(dev), _cu(nq).to(dev), 1, 3000, case.scale)
+    a = g.paged_attention(*args)
+    b = g.paged_attention(*args, softcap=0.0, sliding_window=0, sinks=None)
+    assert torch.equal(a, b)

@@ -202,3 +202,33 @@ def test_q8t_layout_matches_q8_rows():
     b = O.attention_paged(*args, v_rec, bt, lens, 0.088, Hkv, v_fmt="q8t",
                           v_strides=(Hkv * bs * rb, 0, bs * rb), **kw)
     assert np.array_equal(a, b)
+
+
+def test_torch_path_matches_c_oracle():
+    """The torch restatement of the reference's CPU pipeline (gather,
+    dequantize_q8_0, repeat_interleave, SDPA with the causal keep-mask) and
+    the C oracle agree on a mixed decode / prefill batch."""
+    import torch
+    import torch_path as TP
+    rng = np.random.default_rng(5)
+    Hq, Hkv, D, bs = 12, 2, 128, 16
+    lens, nq = [200, 37, 64], [1, 1, 20]
+    NB = sum((L + bs - 1) // bs for L in lens) + 3
+    perm = rng.permutation(NB).astype(np.int32)
+    MB = max((L + bs - 1) // bs for L in lens)
+    bt = np.zeros((len(lens), MB), np.int32)
+    c = 0
+    for b, L in enumerate(lens):
+        n = (L + bs - 1) // bs
+        bt[b, :n] = perm[c:c + n]
+        c += n
+    kc = O.quantize_q8_0(rng.standard_normal((NB, bs, Hkv, D)).astype(np.float16))
+    vc = rng.standard_normal((NB, bs, Hkv, D)).astype(np.float16)
+    q = rng.standard_normal((sum(nq), Hq, D)).astype(np.float16)
+    scale = 1 / np.sqrt(D)
+    nqa = np.array(nq, np.int32)
+    ref = O.attention_paged(q, None, np.concatenate([[0], np.cumsum(nq)[:-1]]).astype(np.int32), nqa, kc, vc, bt,
+                            np.array(lens, np.int32), scale, Hkv, q_abs=np.array(lens, np.int32) - nqa)
+    out = TP.attention_varlen(torch.from_numpy(q), torch.from_numpy(kc), torch.from_numpy(vc), torch.from_numpy(bt),
+                              lens, nq, scale)
+    assert np.abs(out.numpy() - ref).max() < 1e-4
