@@ -345,6 +345,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-mixed", action="store_true", help="skip the config-5 mixed-batch measurement")
     ap.add_argument("--no-kv", action="store_true", help="skip the config-2 KV store + gather measurement")
+    ap.add_argument("--tp-emulate", type=int, default=1,
+                    help="single GPU: run rank 0's kv-head share of N-way tensor parallelism (profiling)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -382,7 +384,9 @@ def main():
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     from gfx906_fa_shard import head_shard
-    shard = head_shard(HQ, HKV, world, rank)      # vLLM-style tensor-parallel head groups
+    # vLLM-style tensor-parallel head groups; --tp-emulate N times rank 0's
+    # share of N-way tensor parallelism on this one GPU (profiling aid)
+    shard = head_shard(HQ, HKV, world, rank) if args.tp_emulate <= 1 else head_shard(HQ, HKV, args.tp_emulate, 0)
     hkv, hq = shard.num_heads_kv, shard.num_heads_q
 
     # ---------------- decode workload (config 3) ----------------------------

@@ -336,8 +336,12 @@ extern "C" cudaError_t gfx906_fa_decode_splitk(const G9AttnBatch* batch, void* w
     d.cpre_g = reinterpret_cast<int*>(w + 256);
     d.opart = reinterpret_cast<float*>(w + 256 + cp);
     d.ml = reinterpret_cast<float2*>(w + 256 + cp + (((rows * dec::D * sizeof(float)) + 255) & ~(size_t)255));
-    cudaError_t ze = cudaMemsetAsync(d.counter, 0, sizeof(unsigned int), stream);
-    if (ze != cudaSuccess) return ze;
+    // the queue-driven kernels claim items from the counter; the transposed
+    // kernels split statically and never read it
+    if (!d.tr) {
+      cudaError_t ze = cudaMemsetAsync(d.counter, 0, sizeof(unsigned int), stream);
+      if (ze != cudaSuccess) return ze;
+    }
   }
   const int vt = batch->v_fmt;
   // general score path: additive mask, soft-cap or sliding window
@@ -401,8 +405,8 @@ extern "C" cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch,
   }
   // Nothing in the array has to be cleared by the caller: the work-queue
   // counter at its start is zeroed by the call itself (cudaMemsetAsync on the
-  // stream), and every partial result the combine step reads is written
-  // earlier in the same call.
+  // stream) whenever the chosen kernel reads it, and every partial result the
+  // combine step reads is written earlier in the same call.
   return gfx906_fa_decode_splitk(batch, ptr, kNoAllocScratchBytes, stream);
 }
 

@@ -43,11 +43,51 @@ struct StoreArgs {
   int v_store_w;                // same for V rows
   int vec_ok_k, vec_ok_v;       // 1 when 4-element vector loads are aligned
   int hkv_log2, bs_log2;        // fast path: log2 of Hkv and block size (powers of two)
+  // fused RoPE (rope_store_kernel only)
+  void* query;                  // [T, Hq, D], rotated in place (may be null)
+  int q_dt, Hq;
+  int64_t q_tok, q_head;        // elements
+  const int64_t* positions;     // [T]
+  const void* cos_sin;          // [max_pos, rot]: cos of pair j at j, sin at rot/2 + j
+  int cs_dt, rot, neox;
 };
 
 constexpr int kWarps = 8;
 constexpr int kMaxD = 512;
 constexpr int kStage = ((kMaxD / QK) * QBLOCK + 7) & ~7;   // 544 bytes per warp
+
+// Quantise the 4 elements v of this lane (elements e0 .. e0+3 of a row; a
+// 32-element block spans 8 lanes) into their Q8_0 block in `stage`.  Every
+// lane of the warp must call it (the block absmax is a shuffle reduction);
+// inactive lanes pass zeros.
+__device__ __forceinline__ void quant4_to_stage(const float v[4], int e0, bool active, uint8_t* stage) {
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  const float d = amax / 127.0f;
+  const float id = d > 0.0f ? __frcp_rn(d) : 0.0f;
+  if (active) {
+    const int blk = e0 / QK;                 // block index within the row
+    const int j = (e0 % QK) / 4;             // lane slot within the block (0..7)
+    uint8_t* out = stage + blk * QBLOCK;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int qi = __float2int_rn(v[i] * id);
+      qi = max(-128, min(127, qi));
+      packed |= (uint32_t)(qi & 0xff) << (8 * i);
+    }
+    // byte offset 2 + 4j is 2-aligned: two 16-bit stores
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * j);
+    o16[0] = (uint16_t)(packed & 0xffffu);
+    o16[1] = (uint16_t)(packed >> 16);
+    if (j == 0) {
+      __half dh = __float2half_rn(d);
+      *reinterpret_cast<uint16_t*>(out) = __half_as_ushort(dh);
+    }
+  }
+}
 
 // Quantise one row of D elements held as 4 elements per lane per 128-element
 // chunk and leave the Q8_0 bytes in `stage`.
@@ -66,32 +106,7 @@ __device__ __forceinline__ void quant_row_to_stage(const void* src, int64_t base
         for (int i = 0; i < 4; ++i) v[i] = load_one(src, base + e0 + i, dt);
       }
     }
-    float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-    const float d = amax / 127.0f;
-    const float id = d > 0.0f ? __frcp_rn(d) : 0.0f;
-    if (active) {
-      const int blk = e0 / QK;                 // block index within the row
-      const int j = (e0 % QK) / 4;             // lane slot within the block (0..7)
-      uint8_t* out = stage + blk * QBLOCK;
-      uint32_t packed = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        int qi = __float2int_rn(v[i] * id);
-        qi = max(-128, min(127, qi));
-        packed |= (uint32_t)(qi & 0xff) << (8 * i);
-      }
-      // byte offset 2 + 4j is 2-aligned: two 16-bit stores
-      uint16_t* o16 = reinterpret_cast<uint16_t*>(out + 2 + 4 * j);
-      o16[0] = (uint16_t)(packed & 0xffffu);
-      o16[1] = (uint16_t)(packed >> 16);
-      if (j == 0) {
-        __half dh = __float2half_rn(d);
-        *reinterpret_cast<uint16_t*>(out) = __half_as_ushort(dh);
-      }
-    }
+    quant4_to_stage(v, e0, active, stage);
   }
   __syncwarp();
 }
@@ -109,6 +124,46 @@ __device__ __forceinline__ void stage_to_global(const uint8_t* stage, uint8_t* d
       reinterpret_cast<uint16_t*>(dst)[i] = reinterpret_cast<const uint16_t*>(stage)[i];
   }
   __syncwarp();
+}
+
+// V row of (token t, head h) into slot (blk, off) per v_mode: Q8_0 token row
+// (2), page-transposed Q8_0 record (3), or a 16-bit copy (1).  `stage` is
+// the warp's shared-memory row buffer.
+__device__ __forceinline__ void store_v_row(const StoreArgs& a, int t, int h, int64_t blk, int64_t off,
+                                            uint8_t* stage) {
+  const int rb = q8_row_bytes(a.D);
+  if (a.v_mode == 2) {
+    quant_row_to_stage(a.value, (int64_t)t * a.val_tok + (int64_t)h * a.val_head, a.val_dt, a.D,
+                       a.vec_ok_v, stage);
+    stage_to_global(stage, a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head, rb,
+                    a.v_store_w);
+  } else if (a.v_mode == 3) {
+    // page-transposed record of (page, head): fp16 scales [D/32][bs], then
+    // int8 values [D][bs]
+    quant_row_to_stage(a.value, (int64_t)t * a.val_tok + (int64_t)h * a.val_head, a.val_dt, a.D,
+                       a.vec_ok_v, stage);
+    uint8_t* rec = a.v_cache + blk * a.vc_blk + h * a.vc_head;
+    const int nb = a.D / QK;
+    const int lane = lane_id();
+    for (int j = lane; j < nb; j += 32)
+      *reinterpret_cast<uint16_t*>(rec + 2 * ((int64_t)j * a.bs + off)) =
+          *reinterpret_cast<const uint16_t*>(stage + j * QBLOCK);
+    uint8_t* qv = rec + 2 * nb * a.bs + off;
+    for (int i = lane; i < a.D; i += 32) qv[(int64_t)i * a.bs] = stage[(i / QK) * QBLOCK + 2 + (i % QK)];
+    __syncwarp();
+  } else if (a.v_mode == 1) {
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) +
+                          (int64_t)t * a.val_tok + (int64_t)h * a.val_head;
+    uint8_t* dst = a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head;
+    const int lane = lane_id();
+    if (a.v_store_w == 8 && a.vec_ok_v) {
+      for (int i = lane; i < a.D / 4; i += 32)
+        reinterpret_cast<uint2*>(dst)[i] = reinterpret_cast<const uint2*>(src)[i];
+    } else {
+      for (int i = lane; i < a.D; i += 32)
+        reinterpret_cast<uint16_t*>(dst)[i] = src[i];
+    }
+  }
 }
 
 __global__ void __launch_bounds__(kWarps * 32) q8_store_kernel(StoreArgs a) {
@@ -129,38 +184,7 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_kernel(StoreArgs a) {
     stage_to_global(stage, a.k_cache + blk * a.kc_blk + off * a.kc_tok + h * a.kc_head, rb,
                     a.k_store_w);
     // ---- V -----------------------------------------------------------------
-    if (a.v_mode == 2) {
-      quant_row_to_stage(a.value, (int64_t)t * a.val_tok + (int64_t)h * a.val_head, a.val_dt, a.D,
-                         a.vec_ok_v, stage);
-      stage_to_global(stage, a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head, rb,
-                      a.v_store_w);
-    } else if (a.v_mode == 3) {
-      // page-transposed record of (page, head): fp16 scales [D/32][bs], then
-      // int8 values [D][bs]
-      quant_row_to_stage(a.value, (int64_t)t * a.val_tok + (int64_t)h * a.val_head, a.val_dt, a.D,
-                         a.vec_ok_v, stage);
-      uint8_t* rec = a.v_cache + blk * a.vc_blk + h * a.vc_head;
-      const int nb = a.D / QK;
-      const int lane = lane_id();
-      for (int j = lane; j < nb; j += 32)
-        *reinterpret_cast<uint16_t*>(rec + 2 * ((int64_t)j * a.bs + off)) =
-            *reinterpret_cast<const uint16_t*>(stage + j * QBLOCK);
-      uint8_t* qv = rec + 2 * nb * a.bs + off;
-      for (int i = lane; i < a.D; i += 32) qv[(int64_t)i * a.bs] = stage[(i / QK) * QBLOCK + 2 + (i % QK)];
-      __syncwarp();
-    } else if (a.v_mode == 1) {
-      const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) +
-                            (int64_t)t * a.val_tok + (int64_t)h * a.val_head;
-      uint8_t* dst = a.v_cache + blk * a.vc_blk + off * a.vc_tok + h * a.vc_head;
-      const int lane = lane_id();
-      if (a.v_store_w == 8 && a.vec_ok_v) {
-        for (int i = lane; i < a.D / 4; i += 32)
-          reinterpret_cast<uint2*>(dst)[i] = reinterpret_cast<const uint2*>(src)[i];
-      } else {
-        for (int i = lane; i < a.D; i += 32)
-          reinterpret_cast<uint16_t*>(dst)[i] = src[i];
-      }
-    }
+    store_v_row(a, t, h, blk, off, stage);
   }
 }
 
@@ -264,6 +288,104 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast_kernel(StoreArgs a)
         reinterpret_cast<uint64_t*>(a.k_cache + kdst[i])[lane] =
             reinterpret_cast<const uint64_t*>(stage + i * kFastRowBytes)[lane];
     __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Fused RoPE + KV store (head_dim 128).  The rows of K (T x Hkv) and of Q
+// (T x Hq) are one grid-stride list: a K row is rotated, rounded once to
+// its element type and written back in place (the rotated key the unfused
+// rotary op would leave), then quantised to Q8_0 into the cache by slot with
+// its V row stored per v_mode; a Q row is rotated and written back.  Lane l
+// holds elements 4l .. 4l+3.  Rotation, in fp32 with separately rounded
+// products (no FMA contraction), for pair (x, y) with angle cos c / sin s:
+//   x' = x*c - y*s,  y' = y*c + x*s
+// NeoX style pairs element i with i + rot/2 (partner lane l ^ rot/8);
+// GPT-J style pairs 2j with 2j+1 (inside a lane).  Elements >= rot are not
+// rotated.  cos/sin of pair j at position p: cos_sin[p*rot + j] and
+// cos_sin[p*rot + rot/2 + j] (vLLM's cos_sin_cache).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float round_to(float x, int dt) {
+  if (dt == DT_F16) return __half2float(__float2half_rn(x));
+  if (dt == DT_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  return x;
+}
+
+__device__ __forceinline__ void store_four(void* p, int64_t i, int dt, const float v[4]) {
+  if (dt == DT_F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p) + i) = make_float4(v[0], v[1], v[2], v[3]);
+  } else if (dt == DT_F16) {
+    __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  } else {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p) + i) =
+        make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+}
+
+__device__ __forceinline__ void rope4(const StoreArgs& a, int64_t pos, int lane, float v[4]) {
+  const int rot = a.rot, half = rot >> 1;
+  const int64_t cb = pos * rot;
+  const int e0 = 4 * lane;
+  if (a.neox) {
+    float p[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p[k] = __shfl_xor_sync(0xffffffffu, v[k], half >> 2);
+    if (e0 < rot) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = e0 + k;
+        const int j = i < half ? i : i - half;
+        const float c = load_one(a.cos_sin, cb + j, a.cs_dt), s = load_one(a.cos_sin, cb + half + j, a.cs_dt);
+        v[k] = i < half ? __fsub_rn(__fmul_rn(v[k], c), __fmul_rn(p[k], s))
+                        : __fadd_rn(__fmul_rn(v[k], c), __fmul_rn(p[k], s));
+      }
+    }
+  } else if (e0 < rot) {
+#pragma unroll
+    for (int k = 0; k < 4; k += 2) {
+      const int j = (e0 + k) >> 1;
+      const float c = load_one(a.cos_sin, cb + j, a.cs_dt), s = load_one(a.cos_sin, cb + half + j, a.cs_dt);
+      const float x = v[k], y = v[k + 1];
+      v[k] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+      v[k + 1] = __fadd_rn(__fmul_rn(y, c), __fmul_rn(x, s));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kWarps * 32) rope_store_kernel(StoreArgs a) {
+  __shared__ __align__(16) uint8_t stage_all[kWarps][kFastRowBytes];
+  uint8_t* stage = stage_all[warp_id()];
+  const int lane = lane_id();
+  const int64_t rows_k = (int64_t)a.T * a.Hkv;
+  const int64_t rows = rows_k + (a.query ? (int64_t)a.T * a.Hq : 0);
+  for (int64_t row = (int64_t)blockIdx.x * kWarps + warp_id(); row < rows; row += (int64_t)gridDim.x * kWarps) {
+    const bool isk = row < rows_k;
+    const int64_t r = isk ? row : row - rows_k;
+    const int H = isk ? a.Hkv : a.Hq;
+    const int t = (int)(r / H), h = (int)(r % H);
+    void* src = isk ? const_cast<void*>(a.key) : a.query;
+    const int dt = isk ? a.key_dt : a.q_dt;
+    const int64_t base = isk ? (int64_t)t * a.key_tok + (int64_t)h * a.key_head
+                             : (int64_t)t * a.q_tok + (int64_t)h * a.q_head;
+    float v[4];
+    load_four(src, base + 4 * lane, dt, v);
+    rope4(a, a.positions[t], lane, v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = round_to(v[k], dt);
+    store_four(src, base + 4 * lane, dt, v);
+    if (!isk) continue;
+    const int64_t slot = a.slot_mapping[t];
+    // the whole warp takes the branch together (slot is per row)
+    if (slot < 0) continue;
+    const int64_t blk = slot / a.bs, off = slot % a.bs;
+    quant4_to_stage(v, 4 * lane, true, stage);
+    __syncwarp();
+    stage_to_global(stage, a.k_cache + blk * a.kc_blk + off * a.kc_tok + h * a.kc_head, kFastRowBytes,
+                    a.k_store_w);
+    store_v_row(a, t, h, blk, off, stage);
   }
 }
 
@@ -383,4 +505,53 @@ extern "C" cudaError_t gfx906_fa_store_kv(
     a.vec_ok_v = vec_aligned(value, value_dtype, value_token_stride, value_head_stride);
   }
   return launch_store(a, stream);
+}
+
+extern "C" cudaError_t gfx906_fa_rope_store_kv(
+    void* query, int query_dtype, int64_t query_token_stride, int64_t query_head_stride, int num_heads_q,
+    void* key, int key_dtype, int64_t key_token_stride, int64_t key_head_stride, const void* value,
+    int value_dtype, int64_t value_token_stride, int64_t value_head_stride, const int64_t* positions,
+    const void* cos_sin_cache, int cos_sin_dtype, int rot_dim, int is_neox, const int64_t* slot_mapping,
+    uint8_t* k_cache, int64_t k_block_stride, int64_t k_token_stride, int64_t k_head_stride, uint8_t* v_cache,
+    int64_t v_block_stride, int64_t v_token_stride, int64_t v_head_stride, int v_mode, int num_tokens,
+    int num_kv_heads, int head_size, int block_size, cudaStream_t stream) {
+  if (head_size != 128 || num_tokens < 0 || num_kv_heads <= 0 || block_size <= 0) return cudaErrorInvalidValue;
+  if (!(rot_dim == 32 || rot_dim == 64 || rot_dim == 128)) return cudaErrorInvalidValue;
+  if (key_dtype < 0 || key_dtype > 2 || cos_sin_dtype < 0 || cos_sin_dtype > 2 || v_mode < 0 || v_mode > 3)
+    return cudaErrorInvalidValue;
+  if (query && (num_heads_q <= 0 || query_dtype < 0 || query_dtype > 2)) return cudaErrorInvalidValue;
+  if (!key || !positions || !cos_sin_cache || !slot_mapping || !k_cache) return cudaErrorInvalidValue;
+  if (v_mode != G9_V_NONE && (value == nullptr || v_cache == nullptr)) return cudaErrorInvalidValue;
+  if (v_mode == G9_V_COPY16 && value_dtype == G9_DT_F32) return cudaErrorInvalidValue;
+  if (v_mode == G9_V_Q8T && (((uintptr_t)v_cache | (uintptr_t)v_block_stride | (uintptr_t)v_head_stride) & 1))
+    return cudaErrorInvalidValue;
+  // rows are read and written as 4-element vectors
+  if (!vec_aligned(key, key_dtype, key_token_stride, key_head_stride) ||
+      (query && !vec_aligned(query, query_dtype, query_token_stride, query_head_stride)))
+    return cudaErrorInvalidValue;
+  if (num_tokens == 0) return cudaSuccess;
+  StoreArgs a{};
+  const int rb = q8_row_bytes(head_size);
+  a.key = key; a.key_dt = key_dtype; a.key_tok = key_token_stride; a.key_head = key_head_stride;
+  a.value = value; a.val_dt = value_dtype; a.val_tok = value_token_stride; a.val_head = value_head_stride;
+  a.slot_mapping = slot_mapping;
+  a.k_cache = k_cache; a.kc_blk = k_block_stride; a.kc_tok = k_token_stride; a.kc_head = k_head_stride;
+  a.v_cache = v_cache; a.vc_blk = v_block_stride; a.vc_tok = v_token_stride; a.vc_head = v_head_stride;
+  a.v_mode = v_mode;
+  a.T = num_tokens; a.Hkv = num_kv_heads; a.D = head_size; a.bs = block_size;
+  a.k_store_w = store_width(k_cache, k_block_stride, k_token_stride, k_head_stride, rb);
+  if (v_mode == G9_V_Q8 || v_mode == G9_V_Q8T) {
+    a.v_store_w = store_width(v_cache, v_block_stride, v_token_stride, v_head_stride, rb);
+    a.vec_ok_v = vec_aligned(value, value_dtype, value_token_stride, value_head_stride);
+  } else if (v_mode == G9_V_COPY16) {
+    a.v_store_w = store_width(v_cache, v_block_stride, v_token_stride, v_head_stride, 2 * head_size);
+    a.vec_ok_v = vec_aligned(value, value_dtype, value_token_stride, value_head_stride);
+  }
+  a.query = query; a.q_dt = query_dtype; a.q_tok = query_token_stride; a.q_head = query_head_stride;
+  a.Hq = num_heads_q;
+  a.positions = positions; a.cos_sin = cos_sin_cache; a.cs_dt = cos_sin_dtype; a.rot = rot_dim;
+  a.neox = is_neox ? 1 : 0;
+  const int64_t rows = (int64_t)num_tokens * (num_kv_heads + (query ? num_heads_q : 0));
+  rope_store_kernel<<<grid_for_rows(rows), kWarps * 32, 0, stream>>>(a);
+  return cudaGetLastError();
 }

@@ -202,6 +202,85 @@ void store_kv(torch::Tensor key, torch::Tensor value, torch::Tensor slot_mapping
 }
 
 // ---------------------------------------------------------------------------
+// rope_store_kv: fused RoPE (query and key rotated in place) + KV store (new)
+// ---------------------------------------------------------------------------
+void rope_store_kv(c10::optional<torch::Tensor> query, torch::Tensor key, torch::Tensor value,
+                   torch::Tensor positions, torch::Tensor cos_sin_cache, bool is_neox, torch::Tensor slot_mapping,
+                   torch::Tensor k_cache, torch::Tensor v_cache, int64_t v_mode) {
+  CHECK_CUDA(key);
+  CHECK_CUDA(positions);
+  CHECK_CUDA(cos_sin_cache);
+  CHECK_CUDA(slot_mapping);
+  CHECK_CUDA(k_cache);
+  const int kdt = dtype_code(key, "key");
+  TORCH_CHECK(key.dim() == 3 && key.stride(2) == 1, "key must be [T, Hkv, D] with contiguous D");
+  const int T = key.size(0), Hkv = key.size(1), D = key.size(2);
+  TORCH_CHECK(D == 128, "head_size must be 128");
+  TORCH_CHECK(positions.dtype() == torch::kInt64 && positions.dim() == 1 && positions.size(0) >= T &&
+                  positions.is_contiguous(), "positions must be contiguous int64 [>= T]");
+  TORCH_CHECK(slot_mapping.dtype() == torch::kInt64 && slot_mapping.dim() == 1 && slot_mapping.size(0) == T &&
+                  slot_mapping.is_contiguous(), "slot_mapping must be contiguous int64 [T]");
+  TORCH_CHECK(cos_sin_cache.dim() == 2 && cos_sin_cache.is_contiguous(), "cos_sin_cache must be [max_pos, rot_dim]");
+  const int csdt = dtype_code(cos_sin_cache, "cos_sin_cache");
+  const int rot = cos_sin_cache.size(1);
+  TORCH_CHECK(rot == 32 || rot == 64 || rot == 128, "rot_dim must be 32, 64 or 128, got ", rot);
+  TORCH_CHECK(v_mode >= 0 && v_mode <= 3, "v_mode must be 0..3");
+  void* qptr = nullptr;
+  int qdt = G9_DT_F16, Hq = 0;
+  int64_t qts = 0, qhs = 0;
+  if (query.has_value()) {
+    auto q = query.value();
+    CHECK_CUDA(q);
+    TORCH_CHECK(q.dim() == 3 && q.size(0) >= T && q.size(2) == D && q.stride(2) == 1,
+                "query must be [>= T, Hq, D] with contiguous D");
+    qdt = dtype_code(q, "query");
+    qptr = q.data_ptr();
+    Hq = q.size(1);
+    qts = q.stride(0);
+    qhs = q.stride(1);
+  }
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(2) == Hkv, "k_cache must be [NB, bs, Hkv, row]");
+  const int bs = k_cache.size(1);
+  const int64_t ke = k_cache.element_size();
+  const void* vptr = nullptr;
+  int vdt = G9_DT_F16;
+  int64_t vts = 0, vhs = 0, vb0 = 0, vb1 = 0, vb2 = 0;
+  uint8_t* vc = nullptr;
+  if (v_mode != 0) {
+    CHECK_CUDA(value);
+    CHECK_CUDA(v_cache);
+    vdt = dtype_code(value, "value");
+    TORCH_CHECK(value.dim() == 3 && value.size(0) == T && value.size(1) == Hkv && value.size(2) == D &&
+                    value.stride(2) == 1, "value must be [T, Hkv, D] with contiguous D");
+    vptr = value.data_ptr();
+    vts = value.stride(0);
+    vhs = value.stride(1);
+    if (v_mode == G9_V_Q8T) {
+      TORCH_CHECK(v_cache.dim() == 3 && v_cache.size(1) == Hkv && v_cache.dtype() == torch::kUInt8,
+                  "v_cache must be uint8 [NB, Hkv, record]");
+      vb0 = v_cache.stride(0);
+      vb2 = v_cache.stride(1);
+    } else {
+      TORCH_CHECK(v_cache.dim() == 4 && v_cache.size(1) == bs && v_cache.size(2) == Hkv,
+                  "v_cache must be [NB, bs, Hkv, row]");
+      const int64_t ve = v_cache.element_size();
+      vb0 = v_cache.stride(0) * ve;
+      vb1 = v_cache.stride(1) * ve;
+      vb2 = v_cache.stride(2) * ve;
+    }
+    vc = reinterpret_cast<uint8_t*>(v_cache.data_ptr());
+  }
+  c10::cuda::CUDAGuard g(key.device());
+  check_status(gfx906_fa_rope_store_kv(qptr, qdt, qts, qhs, Hq, key.data_ptr(), kdt, key.stride(0), key.stride(1),
+                                       vptr, vdt, vts, vhs, positions.data_ptr<int64_t>(), cos_sin_cache.data_ptr(),
+                                       csdt, rot, is_neox ? 1 : 0, slot_mapping.data_ptr<int64_t>(),
+                                       reinterpret_cast<uint8_t*>(k_cache.data_ptr()), k_cache.stride(0) * ke,
+                                       k_cache.stride(1) * ke, k_cache.stride(2) * ke, vc, vb0, vb1, vb2,
+                                       (int)v_mode, T, Hkv, D, bs, cur_stream()),
+               "gfx906_fa_rope_store_kv");
+}
+
+// ---------------------------------------------------------------------------
 // attention
 // ---------------------------------------------------------------------------
 G9AttnBatch batch_base(const torch::Tensor& key_cache_q8, const torch::Tensor& value_cache, int v_fmt,
@@ -552,6 +631,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Fused KV store by slot_mapping: K -> Q8_0, V copied (v_mode=1) or quantized (v_mode=2)",
         py::arg("key"), py::arg("value"), py::arg("slot_mapping"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("v_mode") = 1);
+  m.def("rope_store_kv", &rope_store_kv,
+        "Fused RoPE + KV store: query / key rotated in place (fp32, rounded once), K -> Q8_0, V per v_mode, "
+        "by slot_mapping",
+        py::arg("query"), py::arg("key"), py::arg("value"), py::arg("positions"), py::arg("cos_sin_cache"),
+        py::arg("is_neox"), py::arg("slot_mapping"), py::arg("k_cache"), py::arg("v_cache"), py::arg("v_mode") = 1);
   m.def("forward", &forward, "FA forward (Q fp32/fp16/bf16, K q8_0, V fp16): fp32 [B, Hq, Sq, D]",
         py::arg("q"), py::arg("k_q8"), py::arg("v_fp16"), py::arg("scale"), py::arg("kv_max") = c10::nullopt,
         py::arg("mask") = c10::nullopt, py::arg("q_abs_offset") = c10::nullopt, py::arg("softcap") = 0.0,

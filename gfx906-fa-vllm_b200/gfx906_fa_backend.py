@@ -232,7 +232,26 @@ class Gfx906FAImpl(AttentionImpl):
         return False
 
     def fused_rope_kvcache_supported(self):
-        return False
+        # RoPE is fused into the Q8_0 store kernel (the legacy mode keeps
+        # vLLM's own cache layout and ops)
+        return not self._legacy
+
+    def do_rope_and_kv_cache_update(self, layer: AttentionLayer, query: torch.Tensor, key: torch.Tensor,
+                                    value: torch.Tensor, positions: torch.Tensor, cos_sin_cache: torch.Tensor,
+                                    is_neox: bool, kv_cache: torch.Tensor, layer_slot_mapping: torch.Tensor):
+        """vLLM's RoPE + KV-cache fusion hook: query and key are rotated in
+        place (fp32 arithmetic, one rounding to the model dtype) and the
+        rotated key is quantised into the cache with V, in one kernel."""
+        slots = layer_slot_mapping if layer_slot_mapping.dtype == torch.int64 else layer_slot_mapping.to(torch.int64)
+        n = slots.shape[0]
+        D = self.head_size
+        q3 = query.view(query.shape[0], -1, D)
+        k3 = key.view(key.shape[0], -1, D)
+        v3 = value.view(value.shape[0], -1, D)
+        pos = positions if positions.dtype == torch.int64 else positions.to(torch.int64)
+        k_q8, v = kv_cache_views(kv_cache, self._v_fmt)
+        gfx906_fa.rope_store_kv(q3[:n], k3[:n], v3[:n], pos, cos_sin_cache, bool(is_neox), slots, k_q8, v,
+                                3 if self._v_fmt == "q8_0" else 1)
 
     # ------------------------------------------------------------------
     # KV cache write

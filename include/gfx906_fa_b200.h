@@ -110,6 +110,26 @@ cudaError_t gfx906_fa_store_kv(const void* key, int key_dtype, int64_t key_token
                                int64_t v_head_stride, int v_mode, int num_tokens, int num_kv_heads,
                                int head_size, int block_size, cudaStream_t stream);
 
+/* Fused RoPE + KV store, the kernel behind vLLM's RoPE / KV-cache fusion
+ * hook (AttentionImpl.do_rope_and_kv_cache_update; the reference backend
+ * has none: extension/gfx906_fa_backend.py:444-445).  K [T, Hkv, 128] and,
+ * when query is not NULL, Q [T, Hq, 128] are rotated in place by the
+ * position's angles (positions int64 [T]; cos_sin_cache [max_pos, rot_dim]
+ * with cos of pair j at column j and sin at rot_dim/2 + j; NeoX style pairs
+ * (i, i + rot_dim/2), GPT-J style (2j, 2j+1); rot_dim 32, 64 or 128),
+ * computed in fp32 and rounded once to the tensor's type; the rotated K is
+ * then quantised to Q8_0 into k_cache and V stored per v_mode, both by
+ * slot_mapping (slot < 0: rotated in place, not stored).  Strides as for
+ * gfx906_fa_store_kv. */
+cudaError_t gfx906_fa_rope_store_kv(
+    void* query, int query_dtype, int64_t query_token_stride, int64_t query_head_stride, int num_heads_q,
+    void* key, int key_dtype, int64_t key_token_stride, int64_t key_head_stride, const void* value,
+    int value_dtype, int64_t value_token_stride, int64_t value_head_stride, const int64_t* positions,
+    const void* cos_sin_cache, int cos_sin_dtype, int rot_dim, int is_neox, const int64_t* slot_mapping,
+    uint8_t* k_cache, int64_t k_block_stride, int64_t k_token_stride, int64_t k_head_stride, uint8_t* v_cache,
+    int64_t v_block_stride, int64_t v_token_stride, int64_t v_head_stride, int v_mode, int num_tokens,
+    int num_kv_heads, int head_size, int block_size, cudaStream_t stream);
+
 /* ----------------------------------------------------------------------- */
 /* Attention over a batch of sequences                                       */
 /* ----------------------------------------------------------------------- */

@@ -270,3 +270,44 @@ def attention_bhsd(q: np.ndarray, q_dtype: str | None, k_q8: np.ndarray, v: np.n
         o_strides=(Hq * Sq * D, D, Sq * D),
         k_strides=(Hkv * Skv * rb, rb, Skv * rb), v_strides=(Hkv * Skv * vb, vb, Skv * vb),
         nthreads=nthreads, bs=max(Skv, 1), v_fmt="q8" if v_q8 else ("bf16" if v.dtype == np.uint16 else "f16"))
+
+
+# --------------------------------------------------------------------------
+# Fused RoPE + store (no reference counterpart: the reference backend has no
+# RoPE fusion, extension/gfx906_fa_backend.py:444-445).  Rotation as vLLM's
+# rotary embedding defines it, computed in fp32 with each product and sum
+# rounded separately, then rounded once to the tensor's element type.
+# --------------------------------------------------------------------------
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns (uint16), round to nearest even (finite inputs)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def rope(x: np.ndarray, dtype: str | None, positions: np.ndarray, cos_sin: np.ndarray, neox: bool) -> np.ndarray:
+    """x [T, H, D] (fp16, fp32, or bf16 as uint16 with dtype="bf16");
+    cos_sin [max_pos, rot] float32 (cos of pair j at j, sin at rot/2 + j).
+    Returns the rotated tensor in x's storage type."""
+    xf = bf16_bits_to_f32(x) if dtype == "bf16" else x.astype(np.float32)
+    xf = xf.copy()
+    rot = cos_sin.shape[1]
+    half = rot // 2
+    cs = cos_sin[np.asarray(positions, np.int64)].astype(np.float32)      # [T, rot]
+    c = cs[:, None, :half]
+    s = cs[:, None, half:]
+    if neox:
+        a, b = xf[..., :half].copy(), xf[..., half:rot].copy()
+        xf[..., :half] = (a * c) - (b * s)
+        xf[..., half:rot] = (b * c) + (a * s)
+    else:
+        a, b = xf[..., 0:rot:2].copy(), xf[..., 1:rot:2].copy()
+        xf[..., 0:rot:2] = (a * c) - (b * s)
+        xf[..., 1:rot:2] = (b * c) + (a * s)
+    if dtype == "bf16":
+        return f32_to_bf16_bits(xf)
+    return xf.astype(x.dtype)
