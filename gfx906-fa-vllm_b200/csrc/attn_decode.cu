@@ -204,8 +204,16 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // only for one n-tile and one kv head per CTA (register budget)
   d.nt = (R + 7) / 8;
   const bool v16 = p.v_fmt == G9_VFMT_F16 || p.v_fmt == G9_VFMT_BF16;
-  d.tr = (vq8t || v16) && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled()
-             ? (vq8t && d.HG == 1 && d.nt == 1 ? NWC_TR : NWC) : 0;
+  // Every transposed batch runs 8 compute warps; at one kv head per CTA each
+  // warp takes two pages per stage (16 pages, below), measured 62.7 us
+  // against 70.3 us for 16 warps of one page each on config 3's one-head
+  // share (the 16-warp geometry spills at its 104-register budget).
+  // GFX906_FA_DECODE_TRW=16 selects that geometry (tuning override).
+  d.tr = (vq8t || v16) && R <= 24 && d.nranks <= kMaxRanksTR && decode_tr_enabled() ? NWC : 0;
+  if (d.tr && vq8t && d.HG == 1 && d.nt == 1) {
+    const char* e = std::getenv("GFX906_FA_DECODE_TRW");
+    if (e && std::atoi(e) == NWC_TR) d.tr = NWC_TR;
+  }
   // 16-bit V tokens per shared-memory group (one copy per group when rows are
   // adjacent): 2, padded, for the 16-row kernel; the transposed kernel takes
   // larger groups (fewer copy requests; its key order keeps the ldmatrix
@@ -241,7 +249,8 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
   // (one m-tile only: with two the registers would spill); else one page per
   // warp with 4 stages, or 3 when 4 do not fit.
-  if (d.tr != NWC_TR && (d.tr ? d.nt == 1 && vq8t : mt == 1) && 2 * d.P <= 8 && need(3, 2 * d.P) <= kSmem) {
+  if (d.tr != NWC_TR && (d.tr ? d.nt == 1 && vq8t : mt == 1) && 2 * d.P <= (d.HG == 1 ? MAXP : 8) &&
+      need(3, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = 3;

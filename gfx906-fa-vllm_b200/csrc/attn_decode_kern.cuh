@@ -55,10 +55,10 @@ constexpr int NTHREADS = 384;               // + warpgroup 2: warp 8 produces, 9
 constexpr int MAXST = 4;                    // max pipeline slots (3 or 4 chosen per launch)
 constexpr int MAXP = 16;                    // max pages per stage
 constexpr int MAXG = 16;                    // max page-slot groups (compute warps / HG)
-// Transposed consumer with one kv head per CTA: 16 compute warps + a
-// producer warpgroup (640 threads launched at 96 registers:
-// 16*32*104 + 4*32*64 = 640*96).  With more heads per CTA it runs with the
-// 8-warp geometry above (two pages per warp).
+// Optional geometry of the transposed consumer at one kv head per CTA
+// (GFX906_FA_DECODE_TRW=16): 16 compute warps + a producer warpgroup (640
+// threads launched at 96 registers: 16*32*104 + 4*32*64 = 640*96).  The
+// default is the 8-warp geometry above with two pages per warp.
 constexpr int NWC_TR = 16;
 constexpr int NTHREADS_TR = 640;
 constexpr int REG_COMPUTE_TR = 104;
@@ -454,15 +454,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
     }
   };
 
-  for (int it = 0;; ++it) {
-    const int slot = it % NST;
-    if (!mbar_wait(&full_bar[slot], (it / NST) & 1)) break;
-    if (meta[slot].done) break;
-    const int item = meta[slot].item[sub];
-    const int page0 = meta[slot].page0[sub];
-    const int npages = meta[slot].npages[sub];
-    const bool last = meta[slot].last[sub] != 0;
-    if (item >= 0 && item != cur_item) {
+  auto begin_item = [&](int item) {
       cur_item = item;
       const int rank = item - sid;
       const int cb = rank / d.HGN, cz = rank - cb * d.HGN;
@@ -481,7 +473,31 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
           if constexpr (MASK) klo[nt][c] = window_lo(p, seq_qpos0(p, cb, cnq, ckv), r / d.G);
         }
       start_item(cb, cz * d.HG + hl);
+  };
+
+  // The stream's first item is known from the prefix sums alone (the
+  // producer's first claim computes the same), so its Q loads go out now and
+  // overlap the first page copies instead of following them.
+  if (sid < NS) {
+    const int64_t u = bal_bound(sid, T, NS);
+    int lo = 0, hi = d.nranks;                  // last rank with cpre <= u, then past empty ranks
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (cpre[mid] <= u) lo = mid; else hi = mid;
     }
+    while (cpre[lo + 1] <= u) ++lo;
+    begin_item(sid + lo);
+  }
+
+  for (int it = 0;; ++it) {
+    const int slot = it % NST;
+    if (!mbar_wait(&full_bar[slot], (it / NST) & 1)) break;
+    if (meta[slot].done) break;
+    const int item = meta[slot].item[sub];
+    const int page0 = meta[slot].page0[sub];
+    const int npages = meta[slot].npages[sub];
+    const bool last = meta[slot].last[sub] != 0;
+    if (item >= 0 && item != cur_item) begin_item(item);
     bool pok[PPW];
     int first_ok = -1;
 #pragma unroll
@@ -712,14 +728,27 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
     }
     fence_barrier_init();
   }
+  // Launched with programmatic stream serialisation: everything above may
+  // overlap the previous kernel's tail; nothing it wrote is read before this
+  // wait.  The dependent combine grid may be scheduled from here on (it waits
+  // for this grid's completion itself).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   if constexpr (TR) {
-    // rank prefix sums (balanced split), one warp: contiguous ranks per lane
+    // rank prefix sums (balanced split): every thread loads the lengths of
+    // some ranks (one parallel pass over the sequences), then warp 0 scans
+    int* cpre = reinterpret_cast<int*>(smem + d.cpre_off);
+    const int n = d.nranks;
+    for (int r = threadIdx.x; r < n; r += blockDim.x) {
+      int real, ps;
+      cpre[r] = rank_units(d, r, real, ps);
+    }
+    __syncthreads();
     if (warp == 0) {
-      int* cpre = reinterpret_cast<int*>(smem + d.cpre_off);
-      const int n = d.nranks, per = (n + 31) / 32;
+      const int per = (n + 31) / 32;
       const int r0 = min(n, lane * per), r1 = min(n, r0 + per);
-      int sum = 0, real, ps;
-      for (int r = r0; r < r1; ++r) sum += rank_units(d, r, real, ps);
+      int sum = 0;
+      for (int r = r0; r < r1; ++r) sum += cpre[r];
       int incl = sum;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -728,9 +757,10 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
       }
       int run = incl - sum;
       for (int r = r0; r < r1; ++r) {
+        const int u = cpre[r];
         cpre[r] = run;
         if (blockIdx.x == 0) d.cpre_g[r] = run;
-        run += rank_units(d, r, real, ps);
+        run += u;
       }
       if (lane == 31) {
         cpre[n] = incl;
@@ -1466,7 +1496,7 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
 // shared memory.
 constexpr int kCombineMaxParts = 1024;
 constexpr int kCombineMaxW = 4;
-constexpr int kCombineRowW = 8;             // warps per row with one row per CTA
+constexpr int kCombineRowW = 8;             // fewest warps per row with one row per CTA
 static __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams d) {
   __shared__ float cm[32];                    // per warp (rows x W <= 32): max
   __shared__ float cl[32];                    // den (relative to that max)
@@ -1474,6 +1504,9 @@ static __global__ void __launch_bounds__(1024) decode_combine_kernel(const Decod
   const G9AttnBatch& p = d.p;
   const int b = blockIdx.y;
   const int h = blockIdx.x;
+  // launched as a programmatic dependent of the decode kernel: wait for its
+  // partial results to be complete and visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int nq = seq_nq(p, b);
   if (nq <= 0 || nq * d.G > d.max_rows) return;
   int nsplit, first;            // partials of this (sequence, head): first slot, count
@@ -1568,6 +1601,25 @@ static __global__ void __launch_bounds__(1024) decode_combine_kernel(const Decod
 // ---------------------------------------------------------------------------
 // launcher (host side), instantiated in the attn_decode_v*.cu files
 // ---------------------------------------------------------------------------
+// Launch with programmatic stream serialisation: the kernel may start while
+// the previous kernel in the stream finishes; it runs griddepcontrol.wait
+// before touching anything that kernel wrote.
+template <typename... Args>
+static cudaError_t launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              const DecodeParams& d) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, d);
+}
+
 static inline int num_sms() {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1612,18 +1664,30 @@ cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int grid = d.tr ? d.nstreams / d.NG : std::max(1, std::min(d.n_items, num_sms()));
-  kern<<<grid, d.tr == dec::NWC_TR ? dec::NTHREADS_TR : dec::NTHREADS, smem, stream>>>(d);
-  e = cudaGetLastError();
+  e = launch_pdl(kern, dim3(grid), dim3(d.tr == dec::NWC_TR ? dec::NTHREADS_TR : dec::NTHREADS), smem, stream, d);
   if (e != cudaSuccess) return e;
   if (d.tr || d.S_max > 1) {   // balanced split: any rank may span streams
+    // same shared-memory carve-out as the decode kernel, so the SMs need no
+    // L1 / shared reconfiguration between the two launches
+    static const cudaError_t carve = cudaFuncSetAttribute(
+        decode_combine_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    (void)carve;
     if ((int64_t)d.p.num_heads_kv * d.p.num_seqs < 2 * num_sms()) {
       // few (head, sequence) pairs: one CTA per query row, 8 warps each
-      decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs, d.max_rows), 32 * kCombineRowW, 0, stream>>>(d);
+      // warps per row: about four partials each (the balanced split gives a
+      // rank about nstreams / nranks + 1 of them), 8 .. 32
+      int rw = kCombineRowW;
+      if (d.tr) {
+        const int est = d.nstreams / std::max(1, d.nranks) + 2;
+        while (rw < 32 && 4 * rw < est) rw *= 2;
+      }
+      e = launch_pdl(decode_combine_kernel, dim3(d.p.num_heads_kv, d.p.num_seqs, d.max_rows), dim3(32 * rw),
+                     0, stream, d);
     } else {
       const int cw = std::max(1, std::min(kCombineMaxW, 32 / d.max_rows));   // warps per row
-      decode_combine_kernel<<<dim3(d.p.num_heads_kv, d.p.num_seqs), 32 * d.max_rows * cw, 0, stream>>>(d);
+      e = launch_pdl(decode_combine_kernel, dim3(d.p.num_heads_kv, d.p.num_seqs), dim3(32 * d.max_rows * cw), 0,
+                     stream, d);
     }
-    e = cudaGetLastError();
   }
   return e;
 }

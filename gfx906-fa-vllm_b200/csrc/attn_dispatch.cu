@@ -125,7 +125,26 @@ int ref_grid_x(int seq_q) {
 cudaError_t run_with_pool(G9AttnBatch& b, const int* kv_max_expanded, int grid_x, int kv_fill, bool flat,
                           cudaStream_t stream) {
   const int B = b.num_seqs;
-  const size_t ws = ws_size_impl(b, nullptr, nullptr, !flat);
+  // When some sequence needs the prefill kernel (every sequence has seq_q
+  // query rows here), its staging is sized per sequence from the actual
+  // context lengths: KV_max is read to the host (one synchronisation of
+  // `stream`) instead of bounding every sequence by the longest.
+  std::vector<int> nq_host, kv_host;
+  const int G = b.num_heads_q / b.num_heads_kv;
+  if (flat || (int64_t)b.seq_q * G > decode_row_cap(b)) {
+    nq_host.assign(B, b.seq_q);
+    kv_host.assign(B, kv_fill);
+    if (kv_max_expanded) {
+      cudaError_t e = cudaMemcpy2DAsync(kv_host.data(), sizeof(int), kv_max_expanded, (size_t)grid_x * sizeof(int),
+                                        sizeof(int), B, cudaMemcpyDeviceToHost, stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+      if (e != cudaSuccess) return e;
+      for (int& k : kv_host) k = std::max(0, std::min(k, b.max_kv));
+    }
+  }
+  const int* nqh = nq_host.empty() ? nullptr : nq_host.data();
+  const int* kvh = kv_host.empty() ? nullptr : kv_host.data();
+  const size_t ws = ws_size_impl(b, nqh, kvh, !flat);
   const size_t ints = align_up((size_t)2 * B * sizeof(int));
   void* mem = nullptr;
   cudaError_t e = cudaMallocAsync(&mem, ws + ints, stream);
@@ -138,7 +157,7 @@ cudaError_t run_with_pool(G9AttnBatch& b, const int* kv_max_expanded, int grid_x
   if (e == cudaSuccess) {
     b.kv_len = kvl;
     if (flat) b.block_table = bt;
-    e = attention_impl(b, nullptr, nullptr, reinterpret_cast<uint8_t*>(mem) + ints, ws, stream, !flat);
+    e = attention_impl(b, nqh, kvh, reinterpret_cast<uint8_t*>(mem) + ints, ws, stream, !flat);
   }
   cudaError_t f = cudaFreeAsync(mem, stream);
   return e != cudaSuccess ? e : f;

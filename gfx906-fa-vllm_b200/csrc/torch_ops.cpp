@@ -532,7 +532,19 @@ torch::Tensor forward_paged_direct(torch::Tensor q, torch::Tensor key_cache_q8, 
   torch::Tensor mask_c, qo_c, sinks_c;
   set_mask_qabs(b, B, Sq, b.max_kv, mask, q_abs_offset, mask_c, qo_c);
   set_features(b, Hq, softcap, sliding_window, sinks, sinks_c, q);
-  run_attention(b, q);
+  // Sequences of Sq*G rows above the decode kernel's cap take the prefill
+  // kernel, whose staging grows with each sequence's visible keys: size it
+  // from the actual lengths (one host read of seq_lens) rather than bounding
+  // every sequence by max_blocks * block_size.
+  if (Sq * (Hq / key_cache_q8.size(2)) > 24) {
+    auto sl_host = seq_lens.to(torch::kCPU);
+    std::vector<int> nqh(B, (int)Sq), kvh(B);
+    for (int64_t i = 0; i < B; ++i)
+      kvh[i] = std::max(0, std::min<int>(sl_host.data_ptr<int32_t>()[i], b.max_kv));
+    run_attention(b, q, nqh.data(), kvh.data());
+  } else {
+    run_attention(b, q);
+  }
   return out;
 }
 
