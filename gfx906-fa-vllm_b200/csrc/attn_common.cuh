@@ -90,8 +90,21 @@ __device__ __forceinline__ float sink_log2(const G9AttnBatch& p, int hq) {
   return p.sinks ? p.sinks[hq] * 1.4426950408889634f : -INFINITY;
 }
 
+// Factor folded into a final output row's normalisation: 1 / *out_scale for
+// fp8 outputs (vLLM's static per-tensor output scale), else 1.
+__device__ __forceinline__ float out_quant_factor(const G9AttnBatch& p) {
+  return p.out_dtype == DT_FP8 ? 1.f / *p.out_scale : 1.f;
+}
+
+__device__ __forceinline__ uint8_t to_fp8(float x) {
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+
 __device__ __forceinline__ void store_out2(void* out, int dt, int64_t off, float a, float b) {
-  if (dt == DT_F32) {
+  if (dt == DT_FP8) {
+    *reinterpret_cast<__nv_fp8x2_storage_t*>(reinterpret_cast<uint8_t*>(out) + off) =
+        __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  } else if (dt == DT_F32) {
     *reinterpret_cast<float2*>(reinterpret_cast<float*>(out) + off) = make_float2(a, b);
   } else if (dt == DT_F16) {
     *reinterpret_cast<__half2*>(reinterpret_cast<__half*>(out) + off) = __floats2half2_rn(a, b);

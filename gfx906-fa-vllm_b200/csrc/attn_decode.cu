@@ -146,8 +146,9 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   if (p.num_seqs < 0 || p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv)
     return cudaErrorInvalidValue;
   if (p.seq_q < 0 || p.max_kv < 0 || p.max_blocks < 0) return cudaErrorInvalidValue;
-  if (p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2 || p.v_fmt < 0 || p.v_fmt > 3)
+  if (p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 3 || p.v_fmt < 0 || p.v_fmt > 3)
     return cudaErrorInvalidValue;
+  if (p.out_dtype == G9_DT_FP8E4M3 && !p.out_scale) return cudaErrorInvalidValue;
   // Q rows are read as pairs of elements (8-byte fp32 / 4-byte 16-bit loads)
   if (((uintptr_t)p.q & 7) || (p.q_seq_stride | p.q_tok_stride | p.q_head_stride) & 1) return cudaErrorInvalidValue;
   d = DecodeParams{};

@@ -429,6 +429,7 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
           const int hq = h * d.G + (r - t * d.G);
           // a sink adds its weight to the denominator once, where the row is final
           if (p.sinks && l > 0.f) inv = 1.f / (l + fast_exp2(sink_log2(p, hq) - mrow[nt][c]));
+          inv *= out_quant_factor(p);
           const int64_t ob = o_offset(p, cb, t, hq);
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt)
@@ -436,7 +437,8 @@ __device__ __forceinline__ void decode_consumer_tr(const DecodeParams& d, uint8_
             for (int hh = 0; hh < 2; ++hh) {
               const float x = (o[nt][mt][2 * hh + c] - cv[mt >> 1][c]) * inv;
               const int64_t off = ob + mt * 16 + hh * 8 + rq;
-              if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = x;
+              if (p.out_dtype == DT_FP8) reinterpret_cast<uint8_t*>(p.out)[off] = to_fp8(x);
+              else if (p.out_dtype == DT_F32) reinterpret_cast<float*>(p.out)[off] = x;
               else if (p.out_dtype == DT_F16) reinterpret_cast<__half*>(p.out)[off] = __float2half_rn(x);
               else reinterpret_cast<__nv_bfloat16*>(p.out)[off] = __float2bfloat16_rn(x);
             }
@@ -1183,6 +1185,7 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
           const int t = r / d.G;
           const int hq = h * d.G + (r - t * d.G);
           if (p.sinks && l > 0.f) inv = 1.f / (l + fast_exp2(sink_log2(p, hq) - mrow[mt][hh]));
+          inv *= out_quant_factor(p);
           const int64_t ob = o_offset(p, cb, t, hq);
 #pragma unroll
           for (int nt = 0; nt < 16; ++nt)
@@ -1590,7 +1593,7 @@ static __global__ void __launch_bounds__(1024) decode_combine_kernel(const Decod
   const int t = r / d.G;
   const int hq = h * d.G + (r - t * d.G);
   if (p.sinks && dsum > 0.f) dsum += fast_exp2(sink_log2(p, hq) - mt);
-  const float inv = dsum > 0.f ? 1.f / dsum : 0.f;
+  const float inv = (dsum > 0.f ? 1.f / dsum : 0.f) * out_quant_factor(p);
   const int64_t off = o_offset(p, b, t, hq) + 4 * lane;
   store_out2(p.out, p.out_dtype, off, nsum.x * inv, nsum.y * inv);
   store_out2(p.out, p.out_dtype, off + 2, nsum.z * inv, nsum.w * inv);

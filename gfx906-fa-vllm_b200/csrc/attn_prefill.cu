@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         tc_fence_after();
         const int g = rg - t * pp.G;
         if (p.sinks && l_run > 0.f) l_run += fast_exp2(sink_log2(p, h * pp.G + g) - m_run);
-        const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+        const float inv = (l_run > 0.f ? 1.f / l_run : 0.f) * out_quant_factor(p);
         const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -750,7 +750,8 @@ static PrefillPlan plan_prefill(const G9AttnBatch& p, int nseq, const int* nq_ca
 static cudaError_t check_prefill_batch(const G9AttnBatch& p) {
   if (p.head_dim != pf::D) return cudaErrorInvalidValue;
   if (p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv) return cudaErrorInvalidValue;
-  if (p.block_size <= 0 || p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 2) return cudaErrorInvalidValue;
+  if (p.block_size <= 0 || p.q_dtype < 0 || p.q_dtype > 2 || p.out_dtype < 0 || p.out_dtype > 3) return cudaErrorInvalidValue;
+  if (p.out_dtype == G9_DT_FP8E4M3 && !p.out_scale) return cudaErrorInvalidValue;
   if (p.v_fmt < 0 || p.v_fmt > 3) return cudaErrorInvalidValue;
   // K rows and Q8_0 V rows are read with 2-byte loads, 16-bit V rows with 4-byte loads
   if (((uintptr_t)p.k_cache | (uintptr_t)p.k_page_stride | (uintptr_t)p.k_tok_stride | (uintptr_t)p.k_head_stride) & 1)

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 
 namespace g9 {
@@ -16,7 +17,7 @@ namespace g9 {
 constexpr int QK = 32;          // elements per Q8_0 block
 constexpr int QBLOCK = 34;      // bytes per Q8_0 block
 
-enum DType : int { DT_F16 = 0, DT_BF16 = 1, DT_F32 = 2 };
+enum DType : int { DT_F16 = 0, DT_BF16 = 1, DT_F32 = 2, DT_FP8 = 3 /* e4m3, outputs only */ };
 
 __host__ __device__ inline int q8_row_bytes(int D) { return (D / QK) * QBLOCK; }
 

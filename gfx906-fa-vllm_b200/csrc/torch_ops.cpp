@@ -560,7 +560,8 @@ torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, t
                               c10::optional<torch::Tensor> out_opt,
                               c10::optional<std::vector<int64_t>> query_lens_host,
                               c10::optional<std::vector<int64_t>> seq_lens_host, double softcap,
-                              int64_t sliding_window, c10::optional<torch::Tensor> sinks) {
+                              int64_t sliding_window, c10::optional<torch::Tensor> sinks,
+                              c10::optional<torch::Tensor> output_scale) {
   CHECK_CUDA(query);
   CHECK_CUDA(query_start_loc);
   TORCH_CHECK(query.dim() == 3 && query.stride(2) == 1, "query must be [T, Hq, D] with contiguous D");
@@ -579,6 +580,7 @@ torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, t
     CHECK_CUDA(out);
     TORCH_CHECK(out.dim() == 3 && out.size(0) >= T && out.size(1) == Hq && out.size(2) == D && out.stride(2) == 1,
                 "out must be [>=T, Hq, D] with contiguous D");
+    TORCH_CHECK(out.device() == query.device(), "out must be on the query's device");
   } else {
     out = torch::empty({T, Hq, D}, query.options());
   }
@@ -595,7 +597,19 @@ torch::Tensor paged_attention(torch::Tensor query, torch::Tensor key_cache_q8, t
   b.flags = G9_F_CU_SEQLENS | G9_F_CAUSAL_END;
   b.seq_q = (int)max_query_len;
   b.out = out.data_ptr();
-  b.out_dtype = dtype_code(out, "out");
+  torch::Tensor oscale_c;
+  if (out.scalar_type() == torch::kFloat8_e4m3fn) {
+    // vLLM's static per-tensor fp8 output quantisation: out = e4m3(o / scale)
+    TORCH_CHECK(output_scale.has_value(), "an fp8 (e4m3) out needs output_scale");
+    oscale_c = output_scale.value().to(torch::kFloat32).reshape({-1}).contiguous();
+    TORCH_CHECK(oscale_c.numel() == 1 && oscale_c.device() == query.device(),
+                "output_scale must be one fp32 value on the query's device");
+    b.out_dtype = G9_DT_FP8E4M3;
+    b.out_scale = oscale_c.data_ptr<float>();
+  } else {
+    TORCH_CHECK(!output_scale.has_value(), "output_scale applies to an fp8 (e4m3) out only");
+    b.out_dtype = dtype_code(out, "out");
+  }
   b.o_tok_stride = out.stride(0);
   b.o_head_stride = out.stride(1);
   b.max_kv = (int)max_seq_len;
@@ -664,7 +678,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("seq_lens"), py::arg("query_start_loc"), py::arg("max_query_len"), py::arg("max_seq_len"),
         py::arg("scale"), py::arg("out") = c10::nullopt, py::arg("query_lens_host") = c10::nullopt,
         py::arg("seq_lens_host") = c10::nullopt, py::arg("softcap") = 0.0, py::arg("sliding_window") = 0,
-        py::arg("sinks") = c10::nullopt);
+        py::arg("sinks") = c10::nullopt, py::arg("output_scale") = c10::nullopt);
   m.def("device_error", &device_error, "Read (and optionally clear) the library's device error word",
         py::arg("clear") = false);
 }

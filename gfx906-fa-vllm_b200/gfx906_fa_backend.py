@@ -82,7 +82,12 @@ class Gfx906FAMetadata:
 
 
 class Gfx906FAMetadataBuilder(AttentionMetadataBuilder[Gfx906FAMetadata]):
-    _cudagraph_support: ClassVar[AttentionCGSupport] = AttentionCGSupport.NEVER
+    # Pure decode batches (one query token per sequence) can be captured in a
+    # CUDA graph: the decode path reads lengths, positions and the block
+    # table from device memory at run time and needs no host value that
+    # changes between replays.  Mixed batches take host-sized prefill
+    # staging and run eagerly.
+    _cudagraph_support: ClassVar[AttentionCGSupport] = AttentionCGSupport.UNIFORM_SINGLE_TOKEN_DECODE
 
     def __init__(self, kv_cache_spec: AttentionSpec, layer_names: list[str], vllm_config: VllmConfig,
                  device: torch.device):
@@ -90,7 +95,12 @@ class Gfx906FAMetadataBuilder(AttentionMetadataBuilder[Gfx906FAMetadata]):
         self.block_size = kv_cache_spec.block_size
 
     def build_for_cudagraph_capture(self, common_attn_metadata: CommonAttentionMetadata) -> Gfx906FAMetadata:
-        return self.build(0, common_attn_metadata)
+        # The kernels clamp each context to max_seq_len; a captured graph is
+        # replayed with longer contexts later, so the bound it bakes in is the
+        # block table's capacity.
+        m = self.build(0, common_attn_metadata)
+        m.max_seq_len = int(m.block_table.shape[1]) * self.block_size
+        return m
 
     def build(self, common_prefix_len: int, common_attn_metadata: CommonAttentionMetadata,
               fast_build: bool = False) -> Gfx906FAMetadata:
@@ -229,7 +239,10 @@ class Gfx906FAImpl(AttentionImpl):
         self._v_fmt = "q8_0" if _V_FMT in ("q8", "q8_0") else "fp16"
 
     def fused_output_quant_supported(self, quant_key):
-        return False
+        # static per-tensor fp8 (e4m3) output quantisation, fused into the
+        # attention epilogues (not on the legacy path)
+        from vllm.model_executor.layers.quantization.utils.quant_utils import kFp8StaticTensorSym
+        return not self._legacy and quant_key == kFp8StaticTensorSym
 
     def fused_rope_kvcache_supported(self):
         # RoPE is fused into the Q8_0 store kernel (the legacy mode keeps
@@ -277,8 +290,10 @@ class Gfx906FAImpl(AttentionImpl):
                 output_scale: torch.Tensor | None = None,
                 output_block_scale: torch.Tensor | None = None) -> torch.Tensor:
         assert output is not None, "Output tensor must be provided."
-        if output_scale is not None or output_block_scale is not None:
-            raise NotImplementedError("GFX906_FA: output quantization is not supported")
+        if output_block_scale is not None:
+            raise NotImplementedError("GFX906_FA: block-scaled output quantization is not supported")
+        if output_scale is not None and self._legacy:
+            raise NotImplementedError("GFX906_FA: output quantization needs the Q8_0 cache path (GFX906_FA_LEGACY=0)")
         if attn_metadata is None:
             return output.fill_(0)                 # profiling run
         assert not attn_metadata.use_cascade, "GFX906_FA: cascade attention is not supported"
@@ -299,7 +314,8 @@ class Gfx906FAImpl(AttentionImpl):
                       attn_metadata.query_start_loc, attn_metadata.max_query_len, attn_metadata.max_seq_len,
                       scale=self.scale, key_cache_q8=k_q8, out=out,
                       query_lens_host=attn_metadata.query_lens_host, seq_lens_host=attn_metadata.seq_lens_host,
-                      softcap=self.logits_soft_cap, sliding_window=self.sliding_window, sinks=self._sinks_f32())
+                      softcap=self.logits_soft_cap, sliding_window=self.sliding_window, sinks=self._sinks_f32(),
+                      output_scale=output_scale)
         return output
 
     def _sinks_f32(self):

@@ -136,6 +136,7 @@ def forward_paged(
     softcap: float = 0.0,
     sliding_window: int = 0,
     sinks: Optional[torch.Tensor] = None,
+    output_scale: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """vLLM-layout paged attention (reference: gfx906_fa_paged.py:197-465).
 
@@ -149,7 +150,9 @@ def forward_paged(
     Beyond the reference: `softcap` (> 0: score -> softcap * tanh(score /
     softcap)), `sliding_window` (> 0: a query at position qp sees keys k with
     qp - k < sliding_window) and `sinks` ([Hq] logits added to each softmax
-    denominator), on every path."""
+    denominator), on every path; `output_scale` with an fp8 (e4m3) `out`:
+    vLLM's static per-tensor output quantisation, out = e4m3(o / scale)
+    (direct path)."""
     num_tokens, Hq, D = query.shape
     num_seqs = block_table.shape[0]
     if scale is None:
@@ -171,10 +174,12 @@ def forward_paged(
         gfx906_fa.paged_attention(query, key_cache_q8, value_cache, bt, sl, cu, int(max_seqlen_q),
                                   int(max_seqlen_k), float(scale), out=o, query_lens_host=query_lens_host,
                                   seq_lens_host=seq_lens_host, softcap=float(softcap),
-                                  sliding_window=int(sliding_window), sinks=sinks)
+                                  sliding_window=int(sliding_window), sinks=sinks, output_scale=output_scale)
         return o if out is not None else o.view(num_tokens, Hq * D)
 
     # ---- gather + flat forward (reference fused / legacy paths) -------------
+    if output_scale is not None:
+        raise NotImplementedError("fp8 output quantisation is implemented on the direct paged path only")
     Sk_pad = ((max_seqlen_k + 31) // 32) * 32
     if key_cache_q8 is not None:
         if _FUSED:

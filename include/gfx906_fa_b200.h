@@ -29,6 +29,8 @@ extern "C" {
 #define G9_DT_F16 0
 #define G9_DT_BF16 1
 #define G9_DT_F32 2
+#define G9_DT_FP8E4M3 3   /* attention output only: out = sat_e4m3(o / *out_scale), vLLM's static
+                             per-tensor fp8 output quantisation */
 
 /* V handling of gfx906_fa_store_kv */
 #define G9_V_NONE 0   /* K only */
@@ -216,6 +218,8 @@ typedef struct G9AttnBatch {
   const float* sinks;   /* [num_heads_q] fp32 logits (scaled-score units) added to each row's softmax
                            denominator only, or NULL */
   int flags;            /* G9_F_* below */
+  const float* out_scale; /* out_dtype G9_DT_FP8E4M3: device fp32 scalar; each output element is
+                             o / *out_scale rounded to e4m3 (nearest even), saturated to +-448 */
 } G9AttnBatch;
 
 /* G9AttnBatch.flags */

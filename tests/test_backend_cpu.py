@@ -94,3 +94,19 @@ def test_kv_cache_views_layout():
 def test_entry_point_declared():
     src = open(os.path.join(PKG, "setup.py")).read()
     assert "vllm.general_plugins" in src and "gfx906_fa = gfx906_fa_backend:register" in src
+
+
+def test_graph_support_and_fused_output_quant_flags():
+    """Pure decode steps may be captured in CUDA graphs; static per-tensor
+    fp8 output quantisation is fused (the reference declared neither)."""
+    be = _backend()
+    from vllm.v1.attention.backend import AttentionCGSupport
+    from vllm.model_executor.layers.quantization.utils.quant_utils import kFp8StaticTensorSym
+    assert be.Gfx906FAMetadataBuilder._cudagraph_support == AttentionCGSupport.UNIFORM_SINGLE_TOKEN_DECODE
+    impl = be.Gfx906FAImpl(num_heads=8, head_size=128, scale=0.1, num_kv_heads=2, alibi_slopes=None,
+                           sliding_window=None, kv_cache_dtype="auto")
+    assert impl.fused_output_quant_supported(kFp8StaticTensorSym)
+    assert impl.fused_rope_kvcache_supported()
+    impl._legacy = True
+    assert not impl.fused_output_quant_supported(kFp8StaticTensorSym)
+    assert not impl.fused_rope_kvcache_supported()
