@@ -38,7 +38,7 @@ class G9AttnBatch(ctypes.Structure):
         ("num_seqs", ctypes.c_int), ("num_heads_q", ctypes.c_int), ("num_heads_kv", ctypes.c_int),
         ("head_dim", ctypes.c_int), ("scale", ctypes.c_float),
         ("num_blocks", ctypes.c_int), ("softcap", ctypes.c_float), ("window", ctypes.c_int),
-        ("sinks", ctypes.c_void_p), ("flags", ctypes.c_int),
+        ("sinks", ctypes.c_void_p), ("flags", ctypes.c_int), ("out_scale", ctypes.c_void_p),
     ]
 
 
