@@ -17,9 +17,11 @@ Differences in how the cache is used:
     tests/test_backend_vs_legacy.py).  Consequence: vLLM code that copies K
     pages as opaque bytes keeps working, code that reads K as 16-bit values
     does not.
-  * V stays in the model dtype (GFX906_FA_V_FMT=fp16, default, the
-    reference's numerics) or is stored as Q8_0 at the start of the V half
-    (GFX906_FA_V_FMT=q8_0).
+  * V stays in the model dtype in the V half (GFX906_FA_V_FMT=fp16, default,
+    the reference's numerics) or (GFX906_FA_V_FMT=q8_0) is stored as Q8_0
+    page-transposed records right after the page's Q8_0 K rows, inside the
+    K half, so a page's K and V are one contiguous byte range
+    (gfx906_fa_paged.kv_cache_views).
   * forward writes straight into vLLM's output buffer in the model dtype:
     no fp32 upcast of the query, no padding, no per-sequence host loop.
   * GFX906_FA_LEGACY=1 keeps the reference's legacy design: 16-bit K/V in
