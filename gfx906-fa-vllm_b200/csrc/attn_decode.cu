@@ -192,13 +192,17 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     if (!vq8t && (hgv % 16 || p.v_tok_stride % 16)) return cudaErrorInvalidValue;
   }
   d.kgs = pad_odd16(4 * hgk);
-  // One or two kv heads per CTA: the copy-request rate of the producer is the
-  // bound (per request cost, not bytes), so a page's K rows (adjacent in HBM)
-  // are copied whole into an unpadded page.  For these row sizes the padded
-  // 4-token groups do not remove bank conflicts anyway (1.5 / 2 wavefronts
-  // per fragment load either way); at 4 and 8 heads the padding halves or
-  // removes them and the rows are copied in 4-token groups.
-  d.kwhole = d.contig && d.HG <= 2;
+  // Up to four kv heads per CTA the copy-request rate of the producer binds
+  // (per request cost, not bytes), so a page's K rows (adjacent in HBM) are
+  // copied whole into an unpadded page.  At one or two heads the padded
+  // 4-token groups remove no bank conflicts anyway (1.5 / 2 wavefronts per
+  // fragment load either way); at four the padding would halve them, but the
+  // fewer copies win (config 3's four-head share: Q8_0 V 211 -> 182 us, fp16 V
+  // 318 -> 292 us).  At eight heads the padded 4-token groups stay (whole-page
+  // copies: Q8_0 V 351 -> 437 us).
+  d.kwhole = d.contig && d.HG <= 4;
+  if (const char* e = std::getenv("GFX906_FA_DECODE_KWHOLE"))      // tuning override: whole-page K copies
+    d.kwhole = d.contig && std::atoi(e) != 0;
   if (d.kwhole) d.kgs = 4 * hgk;
   d.nranks = p.num_seqs * d.HGN;
   // transposed consumer: up to 3 n-tiles of 8 query rows; 16 compute warps

@@ -1510,16 +1510,23 @@ static __global__ void __launch_bounds__(1024) decode_combine_kernel(const Decod
   // launched as a programmatic dependent of the decode kernel: wait for its
   // partial results to be complete and visible
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the sequence's query count and (balanced split) its rank's unit range
+  // are independent loads: issue them together
+  const int rank = b * d.HGN + h / d.HG;
+  int64_t T = 0;
+  int u0 = 0, u1 = 0;
+  if (d.tr) {
+    T = d.cpre_g[d.nranks];
+    u0 = d.cpre_g[rank];
+    u1 = d.cpre_g[rank + 1];
+  }
   const int nq = seq_nq(p, b);
   if (nq <= 0 || nq * d.G > d.max_rows) return;
   int nsplit, first;            // partials of this (sequence, head): first slot, count
   int64_t pstride;              // rows between consecutive partials
   if (d.tr) {
     // balanced split: the streams holding units of this rank
-    const int rank = b * d.HGN + h / d.HG;
-    const int64_t T = d.cpre_g[d.nranks];
     const int NS = (int)(T < d.nstreams ? T : (int64_t)d.nstreams);
-    const int u0 = d.cpre_g[rank], u1 = d.cpre_g[rank + 1];
     if (u1 <= u0) return;
     const int f = bal_sid(u0, T, NS), l = bal_sid(u1 - 1, T, NS);
     nsplit = l - f + 1;
@@ -1544,15 +1551,39 @@ static __global__ void __launch_bounds__(1024) decode_combine_kernel(const Decod
   const int per = (nsplit + W - 1) / W;
   const int s0 = min(nsplit, wi * per), s1 = min(nsplit, s0 + per);
   const int64_t row0 = (int64_t)first * d.R_pad + (active ? r : 0);
+  const float* op = d.opart + row0 * dec::D + 4 * lane;
   float M = -INFINITY;
+  float den = 0.f;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int kFew = 8;
+  if (s1 - s0 <= kFew) {
+    // the usual case: this warp's partials' (max, sum) and output rows are
+    // loaded together, one memory round trip
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (active && s0 + lane < s1) ml = d.ml[row0 + (int64_t)(s0 + lane) * pstride];
+    float4 v[kFew];
+#pragma unroll
+    for (int j = 0; j < kFew; ++j)
+      v[j] = (active && s0 + j < s1) ? *reinterpret_cast<const float4*>(op + (int64_t)(s0 + j) * pstride * dec::D)
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+    M = ml.x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float mu = M == -INFINITY ? 0.f : M;
+    const float w = ml.x == -INFINITY ? 0.f : ml.y * fast_exp2(ml.x - mu);
+    den = w;
+#pragma unroll
+    for (int j = 0; j < kFew; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      num.x = fmaf(wj, v[j].x, num.x); num.y = fmaf(wj, v[j].y, num.y);
+      num.z = fmaf(wj, v[j].z, num.z); num.w = fmaf(wj, v[j].w, num.w);
+    }
+  } else {
   if (active)
     for (int s = s0 + lane; s < s1; s += 32) M = fmaxf(M, d.ml[row0 + (int64_t)s * pstride].x);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   const float mu = M == -INFINITY ? 0.f : M;
-  float den = 0.f;
-  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-  const float* op = d.opart + row0 * dec::D + 4 * lane;
   for (int base = s0; active && base < s1; base += 32) {
     float w = 0.f;
     if (base + lane < s1) {
@@ -1568,6 +1599,7 @@ static __global__ void __launch_bounds__(1024) decode_combine_kernel(const Decod
       num.x = fmaf(wj, v.x, num.x); num.y = fmaf(wj, v.y, num.y);
       num.z = fmaf(wj, v.z, num.z); num.w = fmaf(wj, v.w, num.w);
     }
+  }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
