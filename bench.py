@@ -84,8 +84,9 @@ def config5_work(kv, nq, hkv, hq, v_row):
 # ---------------------------------------------------------------------------
 class ClockSampler:
     """Samples SM clocks and throttle reasons while the timed region runs:
-    NVML polled every 5 ms (so even a region of a few milliseconds gets
-    several samples), nvidia-smi every 200 ms when NVML is not importable."""
+    NVML (opened once, on the calling thread) polled every 5 ms from a
+    background thread and, through sample_until, from the main thread while
+    the queued steps run; nvidia-smi every 200 ms when NVML is unavailable."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -97,6 +98,18 @@ class ClockSampler:
         self.rows = []           # (sm_mhz, max_mhz, set of active reason names)
         self._stop = threading.Event()
         self._t = None
+        self._nv = self._h = None
+        self._max = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self._h = self._handle(nv)
+            self._max = float(nv.nvmlDeviceGetMaxClockInfo(self._h, nv.NVML_CLOCK_SM))
+            self._get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._nv = nv
+        except Exception:
+            self._nv = None
 
     def _handle(self, nv):
         """NVML handle of CUDA device `index` (matched by PCI bus id: NVML
@@ -109,16 +122,14 @@ class ClockSampler:
         except Exception:
             return nv.nvmlDeviceGetHandleByIndex(self.index)
 
-    def _run_nvml(self, nv):
-        h = self._handle(nv)
-        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
-        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            nv.nvmlDeviceGetCurrentClocksThrottleReasons
-        while not self._stop.is_set():
-            sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-            bits = int(get_reasons(h))
-            self.rows.append((sm, mx, {n for n, b in self.REASONS if bits & b}))
-            self._stop.wait(0.005)
+    def _sample_nvml(self):
+        try:
+            nv = self._nv
+            bits = int(self._get_reasons(self._h))
+            self.rows.append((float(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)), self._max,
+                              {n for n, b in self.REASONS if bits & b}))
+        except Exception:
+            pass
 
     def _run_smi(self):
         while not self._stop.is_set():
@@ -136,21 +147,16 @@ class ClockSampler:
             self._stop.wait(0.2)
 
     def _run(self):
-        try:
-            import pynvml as nv
-            nv.nvmlInit()
-        except Exception:
+        if self._nv is None:
             self._run_smi()
             return
-        try:
-            self._run_nvml(nv)
-        except Exception:
-            self._run_smi()
+        while not self._stop.is_set():
+            self._sample_nvml()
+            self._stop.wait(0.005)
 
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
         self._t.start()
-        time.sleep(0.02)                     # first sample before the region starts
         return self
 
     def __exit__(self, *a):
@@ -161,20 +167,11 @@ class ClockSampler:
         """Poll the clocks from this thread until `event` completes (the
         timed region is already queued), so that a region of a few
         milliseconds still gets samples."""
-        try:
-            import pynvml as nv
-            nv.nvmlInit()
-            h = self._handle(nv)
-            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
-            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                nv.nvmlDeviceGetCurrentClocksThrottleReasons
-            while not event.query():
-                bits = int(get_reasons(h))
-                self.rows.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), mx,
-                                  {n for n, b in self.REASONS if bits & b}))
-                time.sleep(0.0002)
-        except Exception:
-            pass
+        if self._nv is None:
+            return
+        while not event.query():
+            self._sample_nvml()
+            time.sleep(0.0002)
 
     def summary(self):
         if not self.rows:

@@ -390,6 +390,23 @@ static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[kNoAllocScratc
 
 #include <mutex>
 
+// The calling thread's current CUDA context (driver handle, through the
+// runtime's driver entry point), or null if it cannot be queried.
+static void* current_context() {
+  typedef int (*CtxGetCurrentFn)(void**);
+  static CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    return (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+               ? reinterpret_cast<CtxGetCurrentFn>(f)
+               : nullptr;
+  }();
+  void* ctx = nullptr;
+  if (fn) fn(&ctx);
+  return ctx;
+}
+
 extern "C" cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch, cudaStream_t stream) {
   if (!batch) return cudaErrorInvalidValue;
   // size check before anything touches the device
@@ -400,20 +417,26 @@ extern "C" cudaError_t gfx906_fa_decode_splitk_noalloc(const G9AttnBatch* batch,
   const size_t need = decode_ws_bytes(d);
   if (need > kNoAllocScratchBytes) return cudaErrorInvalidValue;   // batch too large for the static scratch
   // per-device address of the scratch array, looked up on the first call on
-  // each device (that first call should come before any stream capture)
+  // each device (that first call should come before any stream capture).
+  // The address belongs to the module instance of the context that is
+  // current, so the cache is keyed on that context as well: after a device
+  // reset, or from another context on the same device, it is looked up again.
   constexpr int kMaxDevices = 64;
   static void* addr[kMaxDevices] = {};
+  static void* addr_ctx[kMaxDevices] = {};
   static std::mutex mu;
   int dev = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* ctx = current_context();
   void* ptr = nullptr;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || addr_ctx[dev] != ctx) {
       void* p = nullptr;
       if ((e = cudaGetSymbolAddress(&p, g_decode_noalloc_scratch)) != cudaSuccess) return e;
       addr[dev] = p;
+      addr_ctx[dev] = ctx;
     }
     ptr = addr[dev];
   }

@@ -250,9 +250,12 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast_kernel(StoreArgs a)
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
       // amax / 127 correctly rounded without the IEEE division routine:
-      // y = amax * fl(1/127), then one FMA correction.  Checked exhaustively
-      // (exact rational arithmetic) for every finite fp16 and bf16 value,
-      // which are all the values amax can take here (16-bit inputs).
+      // y = amax * fl(1/127), then one residual-correction step of the
+      // reciprocal product (Markstein's method: r = amax - y*127 exactly by
+      // FMA, y' = y + r*fl(1/127)).  Exact for every finite fp16 and bf16
+      // value, which are all the values amax can take here (16-bit inputs);
+      // tests/test_store_gpu.py::test_fast_store_every_16bit_absmax checks
+      // all of them on the GPU against the oracle's IEEE division.
       constexpr float kInv127 = 1.0f / 127.0f;
       const float y127 = __fmul_rn(amax, kInv127);
       const float dq = fmaf(fmaf(-y127, 127.0f, amax), kInv127, y127);

@@ -193,3 +193,33 @@ def test_rejects_bad_inputs():
         g.reshape_and_cache_q8(torch.zeros((2, 2, 128), dtype=torch.float16, device=dev),
                                torch.zeros(2, dtype=torch.int32, device=dev),
                                torch.zeros((2, 16, 2, 136), dtype=torch.uint8, device=dev))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_fast_store_every_16bit_absmax(dtype):
+    """The fast store kernel computes amax/127 as amax * fl(1/127) plus one
+    FMA residual correction and rounds with the 1.5 * 2^23 add, in place of
+    the IEEE division and rintf of the reference.  Every finite 16-bit value
+    (both signs) is made the absmax of one 32-element block, whose other
+    elements are that value times k/31 rounded to the same type; all Q8_0
+    bytes must equal the oracle's (IEEE division, rintf)."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    if dtype == torch.float16:
+        v = bits.view(np.float16).astype(np.float32)
+    else:
+        v = O.bf16_bits_to_f32(bits)
+    v = v[np.isfinite(v)]
+    n_blk = (len(v) + 511) // 512 * 512                 # whole rows of 4 blocks, whole tokens of 8 heads
+    v = np.concatenate([v, np.zeros(n_blk - len(v), np.float32)])
+    blocks = v[:, None] * (np.arange(32, dtype=np.float32)[::-1] / 31.0)[None, :]   # element 0 = the value
+    rows = blocks.reshape(-1, 128)                      # 4 blocks per 128-element row
+    key = torch.from_numpy(rows).to(dtype).view(-1, 8, 128)
+    T = key.shape[0]
+    NB = (T + 15) // 16
+    cache = torch.zeros((NB, 16, 8, 136), dtype=torch.uint8, device=dev)
+    slots = torch.arange(T, dtype=torch.int64)
+    _gfx().reshape_and_cache_q8(key.to(dev), slots.to(dev), cache)
+    ref = np.zeros((NB, 16, 8, 136), np.uint8)
+    O.reshape_and_cache(to_np(key), slots.numpy(), ref, dtype="bf16" if dtype == torch.bfloat16 else None)
+    got = to_np(cache)
+    assert np.array_equal(got, ref), f"{int((got != ref).sum())} bytes differ"
