@@ -265,12 +265,16 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast_kernel(StoreArgs a)
       // reference, then adding 1.5*2^23 rounds it to an integer with ties to
       // even (exactly rintf for |x| < 2^22) and leaves it in the low mantissa
       // bits; the clamp is applied to the sum, and the int8 is its low byte.
-      // Identical to the general kernel for finite inputs.
+      // Identical to the general kernel for finite inputs.  When the block's
+      // scale underflows so far that 1/d is infinite, a zero element gives
+      // 0 * inf = NaN: it becomes 0, as the general kernel's float -> int
+      // conversion (and the reference's) makes it; +-inf products clamp.
       constexpr float kMagic = 12582912.0f;
       uint32_t rb[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float r = __fadd_rn(__fmul_rn(v[e], id), kMagic);
+        r = r == r ? r : kMagic;
         r = fminf(fmaxf(r, kMagic - 128.0f), kMagic + 127.0f);
         rb[e] = __float_as_uint(r);
       }

@@ -131,6 +131,17 @@ static inline float load_elem(const void* base, int64_t idx, int dtype) {
 /* Q8_0 block quantiser (gfx906_fa_quant.cu:45-85)                          */
 /* ----------------------------------------------------------------------- */
 
+/* float -> int as the GPU converts (the reference kernel's `(int)rintf(q)`
+ * on the device): saturating at the int range, NaN -> 0.  C leaves the
+ * out-of-range and NaN cases undefined; they occur when a block's absmax is
+ * so small that 1/d overflows to infinity (0 * inf = NaN, x * inf = +-inf). */
+static inline int device_f2i(float r) {
+    if (r != r) return 0;
+    if (r >= 2147483647.0f) return 2147483647;
+    if (r <= -2147483648.0f) return -2147483647 - 1;
+    return (int)r;
+}
+
 void q8o_quant_block(const float* v, uint8_t* y) {
     float amax = 0.0f;
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -141,7 +152,7 @@ void q8o_quant_block(const float* v, uint8_t* y) {
     y[1] = (uint8_t)(dh >> 8);
     for (int i = 0; i < 32; ++i) {
         float q = v[i] * id;
-        int qi = (int)rintf(q);
+        int qi = device_f2i(rintf(q));
         if (qi < -128) qi = -128;
         if (qi > 127) qi = 127;
         y[2 + i] = (uint8_t)(int8_t)qi;
