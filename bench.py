@@ -53,6 +53,18 @@ def load_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def tensor_peak(clocks, burst, burst_kind):
+    """Denominator for a tensor-bound region: the sustained (power-capped)
+    GEMM rate when the region's clocks sat below maximum under sw_power_cap,
+    else the burst rate."""
+    sus, sus_kind = sustained_tflops()
+    capped = (clocks.get("sm_mhz") and clocks.get("sm_max_mhz") and "sw_power_cap" in clocks.get("reasons", [])
+              and clocks["sm_mhz"] < 0.97 * clocks["sm_max_mhz"])
+    if capped:
+        return sus, f"{sus_kind} bf16 sustained (clocks power-capped during the region)"
+    return burst, f"{burst_kind} bf16 burst (clocks at maximum during the region)"
+
+
 def sustained_tflops():
     """The measured bf16 GEMM rate under the power cap (seconds-long loop), the
     denominator for a kernel timed inside a long dense step; fallback 1400."""
@@ -623,7 +635,6 @@ def main():
 
     prefill = None
     prefill_clocks = []
-    tf_sus, sus_kind = sustained_tflops()
     if not args.no_prefill:
         del k_cache, v_cache
         torch.cuda.empty_cache()
@@ -631,17 +642,18 @@ def main():
         pms, ws, nch = prefill_run(N, psteps=max(3, args.steps // 4))
         fl_all = prefill_flops(N, 8192, HQ)
         ach = fl_all / world / (pms * 1e-3) / 1e12
-        # the timed prefills run back to back for tens of milliseconds of dense
-        # tensor work: under the 1 kW cap the clocks settle below maximum, so
-        # the denominator is the sustained GEMM rate; the burst fraction is kept
-        # beside it
+        # back-to-back prefills of tens to hundreds of milliseconds of dense
+        # tensor work can settle under the 1 kW cap: the denominator follows
+        # the clocks seen during the region (sustained rate when power-capped,
+        # else burst)
         pc = prefill_clocks[-1]
+        tf_den, den_kind = tensor_peak(pc, tf_peak, peak_kind)
         prefill = {"value": fl_all / (pms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": pms,
                    "workload": f"config4: 1 seq x {N} tokens, 8192-query chunks, causal, GQA 48/8, "
                                f"{'Q8_0' if args.v_fmt.startswith('q8_0') else 'fp16'} V",
                    "workspace_bytes": ws, "clocks": pc,
-                   "roofline": {"bound": "tensor", "achieved": ach, "peak": tf_sus, "unit": "TFLOP/s",
-                                "frac": ach / tf_sus, "peak_kind": f"{sus_kind} bf16 sustained (power-capped)",
+                   "roofline": {"bound": "tensor", "achieved": ach, "peak": tf_den, "unit": "TFLOP/s",
+                                "frac": ach / tf_den, "peak_kind": den_kind,
                                 "frac_of_burst": ach / tf_peak, "burst_peak": tf_peak,
                                 "traffic": (PREFILL_TRAFFIC_PER_FLOP * fl_all / world
                                             if PREFILL_TRAFFIC_PER_FLOP else None),
@@ -651,9 +663,10 @@ def main():
         for NL in [int(x) for x in args.prefill_long.split(",") if x.strip()]:
             lms, lws, _ = prefill_run(NL, psteps=2)
             fl = prefill_flops(NL, 8192, HQ)
+            lden, lkind = tensor_peak(prefill_clocks[-1], tf_peak, peak_kind)
             longer.append({"tokens": NL, "value": fl / (lms * 1e-3) / 1e12, "unit": "TFLOP/s",
                            "ms_per_step": lms, "tflop": fl / 1e12, "workspace_bytes": lws,
-                           "frac": fl / world / (lms * 1e-3) / 1e12 / tf_sus,
+                           "frac": fl / world / (lms * 1e-3) / 1e12 / lden, "peak_kind": lkind,
                            "frac_of_burst": fl / world / (lms * 1e-3) / 1e12 / tf_peak,
                            "clocks": prefill_clocks[-1]})
         if longer:
