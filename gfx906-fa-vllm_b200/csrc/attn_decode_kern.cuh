@@ -1499,7 +1499,6 @@ __global__ void __launch_bounds__(TRW == dec::NWC_TR ? dec::NTHREADS_TR : dec::N
 // shared memory.
 constexpr int kCombineMaxParts = 1024;
 constexpr int kCombineMaxW = 4;
-constexpr int kCombineRowW = 8;             // fewest warps per row with one row per CTA
 static __global__ void __launch_bounds__(1024) decode_combine_kernel(const DecodeParams d) {
   __shared__ float cm[32];                    // per warp (rows x W <= 32): max
   __shared__ float cl[32];                    // den (relative to that max)
@@ -1710,16 +1709,18 @@ cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
     if ((int64_t)d.p.num_heads_kv * d.p.num_seqs < 2 * num_sms()) {
       // few (head, sequence) pairs: one CTA per query row, 8 warps each
       // warps per row: about four partials each (the balanced split gives a
-      // rank about nstreams / nranks + 1 of them), 8 .. 32
-      int rw = kCombineRowW;
-      if (d.tr) {
-        const int est = d.nstreams / std::max(1, d.nranks) + 2;
-        while (rw < 32 && 4 * rw < est) rw *= 2;
-      }
+      // rank about nstreams / nranks + 1 of them), 2 .. 32, so that the grid
+      // stays about one wave of CTAs
+      const int est = d.tr ? d.nstreams / std::max(1, d.nranks) + 2 : d.S_max;
+      int rw = 2;
+      while (rw < 32 && 4 * rw < est) rw *= 2;
       e = launch_pdl(decode_combine_kernel, dim3(d.p.num_heads_kv, d.p.num_seqs, d.max_rows), dim3(32 * rw),
                      0, stream, d);
     } else {
-      const int cw = std::max(1, std::min(kCombineMaxW, 32 / d.max_rows));   // warps per row
+      // warps per row: enough that each takes at most 8 partials (one round
+      // trip of loads), no more, so that the grid stays one wave of CTAs
+      const int est = d.tr ? d.nstreams / std::max(1, d.nranks) + 2 : d.S_max;
+      const int cw = std::max(1, std::min({kCombineMaxW, 32 / d.max_rows, (est + 7) / 8}));
       e = launch_pdl(decode_combine_kernel, dim3(d.p.num_heads_kv, d.p.num_seqs), dim3(32 * d.max_rows * cw), 0,
                      stream, d);
     }
