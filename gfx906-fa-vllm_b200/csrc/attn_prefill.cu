@@ -405,6 +405,7 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
   __shared__ __align__(8) uint64_t bar_vfull[VST], bar_vempty[VST];
   __shared__ __align__(8) uint64_t bar_s[2];     // S_i tile ready (MMA -> softmax i)
   __shared__ __align__(8) uint64_t bar_p[2];     // P_i tile ready (softmax i -> MMA)
+  __shared__ __align__(8) uint64_t bar_ph[2];    // first half of P_i (keys 0..63) ready
   __shared__ __align__(8) uint64_t bar_o[2];     // last PV_i finished
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
@@ -443,7 +444,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
     mbar_init(&bar_q, 1);
     for (int i = 0; i < KST; ++i) { mbar_init(&bar_kfull[i], 1); mbar_init(&bar_kempty[i], 1); }
     for (int i = 0; i < VST; ++i) { mbar_init(&bar_vfull[i], 1); mbar_init(&bar_vempty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&bar_s[i], 1); mbar_init(&bar_p[i], 128); mbar_init(&bar_o[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar_s[i], 1); mbar_init(&bar_p[i], 128); mbar_init(&bar_ph[i], 128); mbar_init(&bar_o[i], 1);
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -494,10 +497,12 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         }
         tc_commit(&bar_s[i]);
       };
-      auto issue_pv = [&](int i, int j) {
+      // half h of O_i += P_i V: keys 64h .. 64h+63 (P columns 32h .. 32h+31)
+      auto issue_pv = [&](int i, int j, int h) {
         const uint32_t v_s = smem_u32(sV + (j % VST) * TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
+        for (int k4 = 0; k4 < BN / 32; ++k4) {
+          const int kk = h * (BN / 32) + k4;
           const uint32_t off = (kk >> 2) * (TILE_BYTES / 2) + (kk & 3) * 32;
           tc_mma_ts(tmem + 256 + i * 128, tmem + i * 128 + kk * 8, sw128_desc(v_s + off), kIdesc,
                     (j > 0 || kk > 0) ? 1u : 0u);
@@ -514,14 +519,22 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         const bool more = j + 1 < nkv;
         if (!mbar_wait(&bar_vfull[j % VST], (j / VST) & 1)) { ok = false; break; }
         if (more && !mbar_wait(&bar_kfull[(j + 1) % KST], ((j + 1) / KST) & 1)) { ok = false; break; }
+        // P_i V starts on the first half of P_i while the softmax still
+        // computes the second half
+        if (!mbar_wait(&bar_ph[0], j & 1)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(0, j, 0);
         if (!mbar_wait(&bar_p[0], j & 1)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(0, j);
+        issue_pv(0, j, 1);
         if (more) issue_s(0, j + 1);
         if (has1) {
+          if (!mbar_wait(&bar_ph[1], j & 1)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(1, j, 0);
           if (!mbar_wait(&bar_p[1], j & 1)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(1, j);
+          issue_pv(1, j, 1);
           if (more) issue_s(1, j + 1);
         }
         tc_commit(&bar_vempty[j % VST]);
@@ -645,6 +658,13 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
             ::"r"(tS + lane_off + c * 8), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]),
               "r"(pk[5]), "r"(pk[6]), "r"(pk[7])
             : "memory");
+        if (c == 3) {
+          // keys 0..63 of P (and any rescale of O above) are in tensor memory:
+          // the first half of P V may start
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bar_ph[wi]);
+        }
       }
       {
         float a0, a1, b0, b1;
