@@ -121,3 +121,33 @@ def test_impl_decode_in_cuda_graph(v_fmt):
                                 h.bt.numpy(), la, 1.0 / np.sqrt(D), Hkv, q_abs=la - 1,
                                 v_fmt="q8" if v_fmt == "q8_0" else "bf16")
         assert_close(to_np(out.float()).reshape(B, Hq, D), ref, what=f"graph replay {step} ({v_fmt})")
+
+
+def test_impl_fused_fp8_output():
+    """Gfx906FAImpl.forward with vLLM's fused static fp8 output quantisation:
+    the output buffer is e4m3 [T, Hq*D] and output_scale a device scalar."""
+    pytest.importorskip("vllm")
+    import gfx906_fa_backend as be
+    from test_paged_gpu import LENS, NQ, _FakeLayer, _Hist, _impl_step
+    h = _Hist(LENS, 8, seed=75, dtype=torch.bfloat16)
+    q, _ = _impl_step(be, h, NQ, "q8_0", False, torch.bfloat16)             # the query of one engine step
+    impl = be.Gfx906FAImpl(num_heads=48, head_size=128, scale=1.0 / np.sqrt(128), num_kv_heads=8, alibi_slopes=None,
+                           sliding_window=None, kv_cache_dtype="auto")
+    impl._v_fmt = "q8_0"
+    kv_cache = torch.zeros((h.NB, 2, 16, 8, 128), dtype=torch.bfloat16, device=dev)
+    impl.do_kv_cache_update(None, h.key.to(dev), h.val.to(dev), kv_cache, h.slots.to(dev))
+    T = sum(NQ)
+    meta = be.Gfx906FAMetadata(num_actual_tokens=T, max_query_len=max(NQ), max_seq_len=max(LENS),
+                               query_start_loc=_cu(NQ).to(dev),
+                               seq_lens=torch.tensor(LENS, dtype=torch.int32, device=dev), block_table=h.bt.to(dev),
+                               slot_mapping=torch.zeros(T, dtype=torch.int64, device=dev),
+                               query_lens_host=list(NQ), seq_lens_host=list(LENS))
+    s = 0.02
+    out = torch.zeros((T, 48 * 128), dtype=torch.float8_e4m3fn, device=dev)
+    impl.forward(_FakeLayer(), q.to(dev), None, None, kv_cache, meta, output=out,
+                 output_scale=torch.tensor(s, dtype=torch.float32, device=dev))
+    got = out.float().cpu().numpy().reshape(T, 48, 128)
+    ref = h.oracle(q, NQ, v_q8=True)
+    err = np.abs(got * s - ref)
+    bound = ATOL + RTOL * np.abs(ref) + s * _e4m3_step(ref / s)
+    assert (err <= bound).all(), f"{int((err > bound).sum())} fp8 outputs out of bound"
