@@ -767,6 +767,28 @@ static PrefillPlan plan_prefill(const G9AttnBatch& p, int nseq, const int* nq_ca
   return pl;
 }
 
+// Sequences run in groups of at most MAXS whose fp16 staging fits kGroupBudget
+// (a single sequence above it forms a group alone); groups run one after the
+// other on the same workspace.  So a batch of many long padded sequences (the
+// reference API's [B, Hq, Sq_pad, D] layout) needs the staging of its largest
+// group, not of the whole batch.  Returns the end of the group starting at base.
+constexpr size_t kGroupBudget = (size_t)1 << 30;
+static int group_end(const G9AttnBatch& p, int nseq, const int* nq_cap, const int* kv_cap, int base) {
+  const int G = p.num_heads_q / p.num_heads_kv;
+  const size_t tile = (size_t)pf::TILE_BYTES * p.num_heads_kv;
+  size_t bytes = 1024;                                  // plan_prefill's total, grown one sequence at a time
+  int end = base;
+  while (end < nseq && end - base < pf::MAXS) {
+    const size_t rt = 2 * (size_t)(((int64_t)nq_cap[end] * G + 2 * pf::BM - 1) / (2 * pf::BM));
+    const size_t kt = (size_t)((kv_cap[end] + pf::BN - 1) / pf::BN);
+    const size_t add = (rt + 2 * kt) * tile;
+    if (end > base && bytes + add > kGroupBudget) break;
+    bytes += add;
+    ++end;
+  }
+  return end;
+}
+
 static cudaError_t check_prefill_batch(const G9AttnBatch& p) {
   if (p.head_dim != pf::D) return cudaErrorInvalidValue;
   if (p.num_heads_kv <= 0 || p.num_heads_q <= 0 || p.num_heads_q % p.num_heads_kv) return cudaErrorInvalidValue;
@@ -787,8 +809,10 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
   using namespace pf;
   cudaError_t e = check_prefill_batch(p);
   if (e != cudaSuccess) return e;
-  for (int base = 0; base < nseq; base += MAXS) {
-    const int n = std::min(MAXS, nseq - base);
+  for (int next = 0; next < nseq;) {
+    const int base = next;
+    const int n = group_end(p, nseq, nq_cap, kv_cap, base) - base;
+    next = base + n;
     PrefillPlan pl = plan_prefill(p, n, nq_cap + base, kv_cap + base);
     if (pl.RT == 0) continue;
     if (!ws || ws_bytes < pl.total) return cudaErrorInvalidValue;
@@ -844,9 +868,10 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
 
 size_t prefill_ws_bytes(const G9AttnBatch& p, int nseq, const int* nq_cap, const int* kv_cap) {
   size_t best = 0;
-  for (int base = 0; base < nseq; base += pf::MAXS) {
-    const int n = std::min(pf::MAXS, nseq - base);
+  for (int base = 0; base < nseq;) {
+    const int n = group_end(p, nseq, nq_cap, kv_cap, base) - base;
     best = std::max(best, plan_prefill(p, n, nq_cap + base, kv_cap + base).total);
+    base += n;
   }
   return best;
 }

@@ -109,3 +109,41 @@ def test_ctypes_batch_matches_c_layout(tmp_path):
     vals = [int(x) for x in subprocess.check_output([str(exe)]).split()]
     assert vals[0] == ctypes.sizeof(G9AttnBatch)
     assert vals[1:] == [getattr(G9AttnBatch, n).offset for n in names]
+
+
+@pytest.mark.skipif(not _built(), reason="library not built")
+def test_prefill_staging_is_bounded_for_padded_batches():
+    """Host-side sizing only (no launch): a config-5-shaped batch in the
+    reference API's padded layout (every sequence has Sq_pad = 4096 query
+    rows) runs its tensor-core sequences in groups whose fp16 staging fits
+    1 GiB, so its workspace stays near the largest group instead of the sum
+    over all 34 sequences (about 9.4 GB); with exact host query lengths the
+    verify rows go to the decode kernel and only the two chunks are staged."""
+    from _util import G9AttnBatch
+    lib = capi()
+    lib.gfx906_fa_attention_workspace_size.restype = ctypes.c_size_t
+    lib.gfx906_fa_attention_workspace_size.argtypes = [ctypes.POINTER(G9AttnBatch), ctypes.c_void_p,
+                                                       ctypes.c_void_p]
+    rng = __import__("numpy").random.default_rng(5)
+    kv = [int(x) for x in rng.integers(16384, 100001, size=32)] + [4096, 24576 + 4096]
+    B, hkv, D, bs, rb = len(kv), 8, 128, 16, 136
+    b = G9AttnBatch()
+    b.q, b.q_dtype = 1 << 20, 2
+    b.q_seq_stride, b.q_tok_stride, b.q_head_stride = 48 * 4096 * D, D, 4096 * D
+    b.seq_q = 4096
+    b.out, b.out_dtype = 2 << 20, 2
+    b.o_seq_stride, b.o_tok_stride, b.o_head_stride = 48 * 4096 * D, D, 4096 * D
+    b.k_cache = 3 << 20
+    b.k_page_stride, b.k_tok_stride, b.k_head_stride = bs * hkv * rb, hkv * rb, rb
+    b.v_cache = 4 << 20
+    b.v_page_stride, b.v_tok_stride, b.v_head_stride = bs * hkv * 2 * D, hkv * 2 * D, 2 * D
+    b.block_table, b.max_blocks, b.block_size = 5 << 20, 6300, bs
+    b.kv_len, b.max_kv = 6 << 20, 6300 * bs
+    b.num_seqs, b.num_heads_q, b.num_heads_kv, b.head_dim = B, 48, hkv, D
+    b.scale = 0.088
+    padded = (ctypes.c_int * B)(*([4096] * B))
+    kvh = (ctypes.c_int * B)(*kv)
+    ws_padded = lib.gfx906_fa_attention_workspace_size(ctypes.byref(b), padded, kvh)
+    exact = (ctypes.c_int * B)(*([4] * 32 + [4096, 4096]))
+    ws_exact = lib.gfx906_fa_attention_workspace_size(ctypes.byref(b), exact, kvh)
+    assert 0 < ws_exact < ws_padded <= (1 << 30) + (64 << 20), (ws_exact, ws_padded)

@@ -148,3 +148,22 @@ def test_config1_golden_prefill_and_decode():
                           out=torch.empty((1, 8, 128), dtype=torch.float32, device=dev))
     assert_close(to_np(o), z["cfg1_decode_out"], what="config 1 decode vs reference")
     assert g.device_error(True) == 0
+
+
+def test_prefill_sequences_in_staging_groups():
+    """Three long-context prefill chunks whose fp16 staging together exceeds
+    the 1 GiB group budget run as two groups, one after the other, on one
+    workspace; every chunk is checked."""
+    lens, nq = [100000, 90000, 80000], [1024, 1024, 1024]
+    case = PagedCase(lens, 8, v_fmt="q8t", seed=61)
+    q = _q((sum(nq), 48, 128), torch.bfloat16, seed=62)
+    out = to_np(_run(case, q, nq, lens).float())
+    qn = to_np(q)
+    rows, seqs, qabs = [], [], []
+    for b, (L, n) in enumerate(zip(lens, nq)):
+        toks = _pick_tokens(n, 12, seed=b)
+        rows += list(b * 1024 + toks)
+        seqs += [b] * len(toks)
+        qabs += list(L - n + toks)
+    rows = np.array(rows)
+    assert_close(out[rows], case.oracle_rows(qn[rows], "bf16", seqs, qabs), what="staging groups")
