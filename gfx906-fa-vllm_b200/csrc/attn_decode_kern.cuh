@@ -1689,7 +1689,9 @@ cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
   }
   if constexpr (MT == 1 && VT <= 1) {
     if (d.tr) {
-      if (d.nt == 1)
+      if (d.nt == 1 && d.ppw == 2)
+        kern = d.nst == 3 ? decode_kernel<1, VT, MASK, 3, 2, dec::NWC, 1> : decode_kernel<1, VT, MASK, 2, 2, dec::NWC, 1>;
+      else if (d.nt == 1)
         kern = d.nst == 4 ? decode_kernel<1, VT, MASK, 4, 1, dec::NWC, 1> : decode_kernel<1, VT, MASK, 3, 1, dec::NWC, 1>;
       else
         kern = d.nst == 4 ? decode_kernel<1, VT, MASK, 4, 1, dec::NWC, 2> : decode_kernel<1, VT, MASK, 3, 1, dec::NWC, 2>;
