@@ -75,6 +75,7 @@ struct PrefillParams {
   int ktile_off[pf::MAXS + 1];
   float scale_log2;
   float cap_in, cap_out;         // soft-cap: scale / softcap and softcap * log2(e) (softcap > 0)
+  int out_vec;                   // output base and strides are 16-byte multiples: staged row stores
   __half* qp;                    // [Hkv][RT*128][128]
   __half* kp;                    // [Hkv][KT*128][128]
   __half* vt;                    // [Hkv][KT][128 d][128 keys]: V^T tiles
@@ -683,17 +684,80 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         const int g = rg - t * pp.G;
         if (p.sinks && l_run > 0.f) l_run += fast_exp2(sink_log2(p, h * pp.G + g) - m_run);
         const float inv = (l_run > 0.f ? 1.f / l_run : 0.f) * out_quant_factor(p);
-        const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
+        if (pp.out_vec) {
+          // Rows are staged in the (now idle) K/V stages, then written as
+          // contiguous 16-byte pieces of each row: a thread-per-row store
+          // touches 32 sectors per warp instruction.  Every MMA has finished
+          // (bar_o follows the last one), so no tensor-core read of the K/V
+          // stages is outstanding.  Row pitch = row bytes + 16: the 16-byte
+          // stores of 8 consecutive rows hit distinct banks.
+          const int es = p.out_dtype == DT_F32 ? 4 : p.out_dtype == DT_FP8 ? 1 : 2;
+          const int rb = D * es;
+          const int pitch = rb + 16;
+          uint8_t* stage = sK + (warp - 4) * 32 * (D * 4 + 16);
+          uint8_t* myrow = stage + lane * pitch;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + lane_off + c * 32, o);
-          tmem_wait_ld();
-          if (row_valid) {
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + lane_off + c * 32, o);
+            tmem_wait_ld();
+            uint32_t w[16];
+            if (p.out_dtype == DT_F32) {
 #pragma unroll
-            for (int e = 0; e < 32; e += 2)
-              store_out2(p.out, p.out_dtype, ob + c * 32 + e, __uint_as_float(o[e]) * inv,
-                         __uint_as_float(o[e + 1]) * inv);
+              for (int q4 = 0; q4 < 8; ++q4) {
+                const float4 v = make_float4(__uint_as_float(o[4 * q4]) * inv, __uint_as_float(o[4 * q4 + 1]) * inv,
+                                             __uint_as_float(o[4 * q4 + 2]) * inv, __uint_as_float(o[4 * q4 + 3]) * inv);
+                *reinterpret_cast<float4*>(myrow + c * 128 + q4 * 16) = v;
+              }
+            } else if (p.out_dtype == DT_FP8) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 4) {
+                const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(
+                    make_float2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv), __NV_SATFINITE, __NV_E4M3);
+                const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(
+                    make_float2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv), __NV_SATFINITE, __NV_E4M3);
+                w[e / 4] = (uint32_t)lo | ((uint32_t)hi << 16);
+              }
+              *reinterpret_cast<uint4*>(myrow + c * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(myrow + c * 32 + 16) = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; e += 2)
+                w[e / 2] = p.out_dtype == DT_F16
+                               ? pack_half2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv)
+                               : pack_bf162(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+                *reinterpret_cast<uint4*>(myrow + c * 64 + q4 * 16) =
+                    make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+            }
+          }
+          __syncwarp();
+          const int cpr = rb / 16;                        // 16-byte pieces per row
+          const int rpi = 32 / cpr;                       // rows per warp instruction
+          const int wrow0 = row0 + wi * BM + (warp & 3) * 32;
+          for (int rr = lane / cpr; rr < 32; rr += rpi) {
+            const int rgw = wrow0 + rr;
+            if (rgw >= R) break;
+            const int tw = rgw / pp.G;
+            const int64_t obw = o_offset(p, b, tw, h * pp.G + (rgw - tw * pp.G)) * es;
+            const int pc = lane % cpr;
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + obw + pc * 16) =
+                *reinterpret_cast<const uint4*>(stage + rr * pitch + pc * 16);
+          }
+        } else {
+          const int64_t ob = row_valid ? o_offset(p, b, t, h * pp.G + g) : 0;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + lane_off + c * 32, o);
+            tmem_wait_ld();
+            if (row_valid) {
+#pragma unroll
+              for (int e = 0; e < 32; e += 2)
+                store_out2(p.out, p.out_dtype, ob + c * 32 + e, __uint_as_float(o[e]) * inv,
+                           __uint_as_float(o[e + 1]) * inv);
+            }
           }
         }
       } else {
@@ -824,6 +888,11 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
     pp.nseq = n;
     pp.min_rows = min_rows;
     pp.scale_log2 = p.scale * kLog2e;
+    {
+      const int64_t es = p.out_dtype == DT_F32 ? 4 : p.out_dtype == DT_FP8 ? 1 : 2;
+      pp.out_vec = (reinterpret_cast<uintptr_t>(p.out) % 16 == 0) && (p.o_seq_stride * es) % 16 == 0 &&
+                   (p.o_tok_stride * es) % 16 == 0 && (p.o_head_stride * es) % 16 == 0;
+    }
     if (p.softcap > 0.f) {
       pp.cap_in = p.scale / p.softcap;
       pp.cap_out = p.softcap * kLog2e;
