@@ -76,6 +76,7 @@ struct PrefillParams {
   float scale_log2;
   float cap_in, cap_out;         // soft-cap: scale / softcap and softcap * log2(e) (softcap > 0)
   int out_vec;                   // output base and strides are 16-byte multiples: staged row stores
+  int v_direct;                  // page-transposed Q8_0 V, 16-token multiple pages, 16-byte aligned records
   __half* qp;                    // [Hkv][RT*128][128]
   __half* kp;                    // [Hkv][KT*128][128]
   __half* vt;                    // [Hkv][KT][128 d][128 keys]: V^T tiles
@@ -109,6 +110,12 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
   const int L = min(seq_len_kv(p, b), (pp.ktile_off[i + 1] - pp.ktile_off[i]) * BN);
   if ((j + 1) * BN <= seq_kv_begin(p, b, nq)) return;  // before every row's window: never read
   __half* kdst = pp.kp + ((int64_t)h * pp.KT + kt) * BN * D;
+  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)D * BN;
+  // Page-transposed Q8_0 V is already [dim][token] inside a page: with pages
+  // of a multiple of 16 tokens and 16-byte aligned records, row d of the V^T
+  // tile is built from 16-byte loads of 16 tokens (one page each) without a
+  // shared-memory transpose.
+  const bool v_direct = pp.v_direct != 0;
   for (int it = threadIdx.x; it < BN * 8; it += blockDim.x) {
     const int key_l = it >> 3;
     const int c = it & 7;                 // 16-element chunk
@@ -133,7 +140,9 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
       }
       const uint8_t* vrow = p.v_cache + (int64_t)phys * p.v_page_stride + off_t * p.v_tok_stride +
                             (int64_t)h * p.v_head_stride;
-      if (p.v_fmt == G9_VFMT_Q8T) {
+      if (v_direct) {
+        // V written below
+      } else if (p.v_fmt == G9_VFMT_Q8T) {
         // page-transposed record: scale (block j, token t) at 2*(j*bs + t),
         // int8 (dim, token t) at 2*(D/32)*bs + dim*bs + t
         const uint8_t* rec = p.v_cache + (int64_t)phys * p.v_page_stride + (int64_t)h * p.v_head_stride;
@@ -169,13 +178,47 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const __grid_constant__ Pr
     uint4* kd = reinterpret_cast<uint4*>(kdst + (int64_t)key_l * D + c * 16);
     kd[0] = reinterpret_cast<uint4*>(kv)[0];
     kd[1] = reinterpret_cast<uint4*>(kv)[1];
-    uint4* vsd = reinterpret_cast<uint4*>(&vs[key_l][c * 16]);
-    vsd[0] = reinterpret_cast<uint4*>(vv)[0];
-    vsd[1] = reinterpret_cast<uint4*>(vv)[1];
+    if (!v_direct) {
+      uint4* vsd = reinterpret_cast<uint4*>(&vs[key_l][c * 16]);
+      vsd[0] = reinterpret_cast<uint4*>(vv)[0];
+      vsd[1] = reinterpret_cast<uint4*>(vv)[1];
+    }
+  }
+  if (v_direct) {
+    // item = (dim d, 16-key group g); a warp covers 32 consecutive dims of one
+    // group: 32 contiguous 16-byte loads when the page holds 16 tokens
+    const int bsz = p.block_size;
+    for (int it = threadIdx.x; it < D * (BN / 16); it += blockDim.x) {
+      const int d = it % D;
+      const int g = it / D;
+      const int key = j * BN + g * 16;
+      __align__(16) __half o16[16];
+      const int phys = key < L ? p.block_table[(int64_t)b * p.max_blocks + key / bsz] : -1;
+      if (key < L && !page_bad(p, phys)) {
+        const int off_t = key % bsz;
+        const uint8_t* rec = p.v_cache + (int64_t)phys * p.v_page_stride + (int64_t)h * p.v_head_stride;
+        const uint4 q = *reinterpret_cast<const uint4*>(rec + 2 * (D / QK) * bsz + (int64_t)d * bsz + off_t);
+        const uint4* sc = reinterpret_cast<const uint4*>(rec + 2 * ((int64_t)(d / QK) * bsz + off_t));
+        __align__(16) __half dv[16];
+        reinterpret_cast<uint4*>(dv)[0] = sc[0];
+        reinterpret_cast<uint4*>(dv)[1] = sc[1];
+        const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+        const int nvalid = min(16, L - key);
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          o16[e] = e < nvalid ? __float2half_rn((float)qb[e] * __half2float(dv[e])) : __float2half_rn(0.f);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) o16[e] = __float2half_rn(0.f);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(vdst + (int64_t)d * BN + g * 16);
+      dst[0] = reinterpret_cast<uint4*>(o16)[0];
+      dst[1] = reinterpret_cast<uint4*>(o16)[1];
+    }
+    return;
   }
   __syncthreads();
   // transposed write: V^T tile [d][key], 8 keys (16 bytes) per item
-  __half* vdst = pp.vt + ((int64_t)h * pp.KT + kt) * (int64_t)D * BN;
   for (int it = threadIdx.x; it < D * (BN / 8); it += blockDim.x) {
     const int d = it / (BN / 8);
     const int k8 = (it % (BN / 8)) * 8;
@@ -892,6 +935,9 @@ cudaError_t run_prefill(const G9AttnBatch& p, int nseq, const int* seq_ids, cons
       const int64_t es = p.out_dtype == DT_F32 ? 4 : p.out_dtype == DT_FP8 ? 1 : 2;
       pp.out_vec = (reinterpret_cast<uintptr_t>(p.out) % 16 == 0) && (p.o_seq_stride * es) % 16 == 0 &&
                    (p.o_tok_stride * es) % 16 == 0 && (p.o_head_stride * es) % 16 == 0;
+      pp.v_direct = p.v_fmt == G9_VFMT_Q8T && p.block_size % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(p.v_cache) % 16 == 0 && p.v_page_stride % 16 == 0 &&
+                    p.v_head_stride % 16 == 0;
     }
     if (p.softcap > 0.f) {
       pp.cap_in = p.scale / p.softcap;

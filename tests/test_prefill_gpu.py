@@ -71,6 +71,21 @@ def test_prefill_v_formats(v_fmt):
     assert_close(to_np(out.float()), case.oracle_varlen(to_np(q), None, nq), what=v_fmt)
 
 
+@pytest.mark.parametrize("bs", [16, 32, 24])
+def test_prefill_q8t_page_sizes(bs):
+    """Page-transposed Q8_0 V staged for the tensor cores: pages of 16 and 32
+    tokens take the direct 16-token loads, 24-token pages the general path;
+    the ragged lengths end inside a 16-token group and inside a key tile."""
+    lens, nq = [1001, 333], [300, 333]
+    case = PagedCase(lens, 8, bs=bs, v_fmt="q8t", seed=3)
+    q = _q((sum(nq), 48, 128), torch.bfloat16, seed=4)
+    out = _gfx().paged_attention(q.to(dev), case.k_cache, case.v_cache, case.block_table.to(dev),
+                                 torch.from_numpy(case.seq_lens).to(dev), _cu(nq).to(dev), max(nq), max(lens),
+                                 case.scale, query_lens_host=nq, seq_lens_host=lens)
+    assert_close(to_np(out.float()), case.oracle_varlen(to_np(q), "bf16", nq), what=f"q8t bs={bs}")
+    assert _gfx().device_error(True) == 0
+
+
 @pytest.mark.parametrize("Sq,Skv", [(1, 64), (7, 300), (64, 64), (200, 512), (512, 1024)])
 def test_flat_forward_sweep(Sq, Skv):
     """gfx906_fa.forward on contiguous [B, Hkv, Skv] K_q8 / V (the gather
