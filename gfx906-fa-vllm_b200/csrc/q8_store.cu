@@ -298,6 +298,104 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast_kernel(StoreArgs a)
   }
 }
 
+// The same store with 16-byte accesses (16-byte aligned K / V rows and V
+// cache): half a warp per row, lane l of the half holding elements 8l ..
+// 8l+7, so a 32-element block is 4 lanes (two shuffles for its absmax) and
+// a warp keeps 8 rows of loads in flight.  Quantisation arithmetic is the
+// one above, element for element.
+constexpr int kRows16 = 8;
+
+__global__ void __launch_bounds__(kWarps * 32) q8_store_fast16_kernel(StoreArgs a) {
+  __shared__ __align__(16) uint8_t stage_all[kWarps][kRows16 * kFastRowBytes];
+  __shared__ int64_t kdst_all[kWarps][kRows16];
+  uint8_t* stage = stage_all[warp_id()];
+  int64_t* kdst_s = kdst_all[warp_id()];
+  const int lane = lane_id();
+  const int half = lane >> 4, hl = lane & 15;
+  const int64_t rows = (int64_t)a.T * a.Hkv;
+  const bool bf_k = a.key_dt == DT_BF16;
+  for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp_id()) * kRows16; r0 < rows;
+       r0 += (int64_t)gridDim.x * kWarps * kRows16) {
+    uint4 kraw[kRows16 / 2], vraw[kRows16 / 2];
+    int64_t kdst[kRows16 / 2], vdst[kRows16 / 2];
+#pragma unroll
+    for (int k = 0; k < kRows16 / 2; ++k) {
+      const int64_t row64 = r0 + 2 * k + half;
+      const bool valid = row64 < rows;
+      const uint32_t row = (uint32_t)row64;
+      const uint32_t t = row >> a.hkv_log2, h = row & ((1u << a.hkv_log2) - 1);
+      const int64_t s = valid ? (a.slot_mapping ? a.slot_mapping[t] : (int64_t)t) : -1;
+      if (s >= 0) {
+        const uint64_t s64 = (uint64_t)s;
+        const uint32_t blk = (uint32_t)(s64 >> a.bs_log2);
+        const uint32_t off = (uint32_t)s64 & ((1u << a.bs_log2) - 1);
+        kdst[k] = (int64_t)((uint64_t)blk * (uint32_t)a.kc_blk + (off * (uint32_t)a.kc_tok + h * (uint32_t)a.kc_head));
+        vdst[k] = (int64_t)((uint64_t)blk * (uint32_t)a.vc_blk + (off * (uint32_t)a.vc_tok + h * (uint32_t)a.vc_head));
+      } else {
+        kdst[k] = vdst[k] = -1;
+      }
+      kraw[k] = valid ? reinterpret_cast<const uint4*>(a.key)[(size_t)row * 16 + hl] : make_uint4(0u, 0u, 0u, 0u);
+      vraw[k] = (valid && a.v_mode == G9_V_COPY16) ? reinterpret_cast<const uint4*>(a.value)[(size_t)row * 16 + hl]
+                                                   : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < kRows16 / 2; ++k) {
+      const uint32_t w[4] = {kraw[k].x, kraw[k].y, kraw[k].z, kraw[k].w};
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (bf_k) {
+          v[2 * e] = __uint_as_float(w[e] << 16); v[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+        } else {
+          const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          v[2 * e] = x.x; v[2 * e + 1] = x.y;
+        }
+      }
+      float amax = fabsf(v[0]);                       // NaN only if every element is NaN, as above
+#pragma unroll
+      for (int e = 1; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+      constexpr float kInv127 = 1.0f / 127.0f;
+      const float y127 = __fmul_rn(amax, kInv127);
+      const float dq = fmaf(fmaf(-y127, 127.0f, amax), kInv127, y127);
+      const float id = dq > 0.0f ? __frcp_rn(dq) : 0.0f;
+      constexpr float kMagic = 12582912.0f;
+      uint32_t rb[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float r = __fadd_rn(__fmul_rn(v[e], id), kMagic);
+        r = r == r ? r : kMagic;
+        r = fminf(fmaxf(r, kMagic - 128.0f), kMagic + 127.0f);
+        rb[e] = __float_as_uint(r);
+      }
+      const uint32_t p0 = __byte_perm(__byte_perm(rb[0], rb[1], 0x0040), __byte_perm(rb[2], rb[3], 0x0040), 0x5410);
+      const uint32_t p1 = __byte_perm(__byte_perm(rb[4], rb[5], 0x0040), __byte_perm(rb[6], rb[7], 0x0040), 0x5410);
+      const int r = 2 * k + half;
+      uint8_t* out = stage + r * kFastRowBytes + (hl >> 2) * QBLOCK;
+      uint16_t* o16 = reinterpret_cast<uint16_t*>(out + 2 + 8 * (hl & 3));
+      o16[0] = (uint16_t)(p0 & 0xffffu);
+      o16[1] = (uint16_t)(p0 >> 16);
+      o16[2] = (uint16_t)(p1 & 0xffffu);
+      o16[3] = (uint16_t)(p1 >> 16);
+      if ((hl & 3) == 0) *reinterpret_cast<uint16_t*>(out) = __half_as_ushort(__float2half_rn(dq));
+      if (hl == 0) kdst_s[r] = kdst[k];
+      if (a.v_mode == G9_V_COPY16 && vdst[k] >= 0)
+        *reinterpret_cast<uint4*>(a.v_cache + vdst[k] + 16 * hl) = vraw[k];
+    }
+    __syncwarp();
+    // the 8 Q8_0 K rows (17 x 8 bytes each) leave as 136 aligned 8-byte stores
+#pragma unroll
+    for (int it = lane; it < kRows16 * (kFastRowBytes / 8); it += 32) {
+      const int r = it / (kFastRowBytes / 8), wd = it - r * (kFastRowBytes / 8);
+      const int64_t kd = kdst_s[r];
+      if (kd >= 0)
+        reinterpret_cast<uint64_t*>(a.k_cache + kd)[wd] = reinterpret_cast<const uint64_t*>(stage + r * kFastRowBytes)[wd];
+    }
+    __syncwarp();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Fused RoPE + KV store (head_dim 128).  The rows of K (T x Hkv) and of Q
 // (T x Hq) are one grid-stride list: a K row is rotated, rounded once to
@@ -433,7 +531,15 @@ cudaError_t launch_store(const StoreArgs& a, cudaStream_t stream) {
     StoreArgs f = a;
     f.hkv_log2 = __builtin_ctzll((unsigned long long)a.Hkv);
     f.bs_log2 = __builtin_ctzll((unsigned long long)a.bs);
-    q8_store_fast_kernel<<<grid_for_rows((rows + kFastRows - 1) / kFastRows), kWarps * 32, 0, stream>>>(f);
+    // 16-byte rows: K (and a copied V) 16-byte aligned, V cache rows too
+    const bool w16 = ((uintptr_t)a.key % 16) == 0 &&
+                     (a.v_mode == G9_V_NONE ||
+                      (((uintptr_t)a.value % 16) == 0 &&
+                       (((uintptr_t)a.v_cache | (uintptr_t)a.vc_blk | (uintptr_t)a.vc_tok | (uintptr_t)a.vc_head) % 16) == 0));
+    if (w16)
+      q8_store_fast16_kernel<<<grid_for_rows((rows + kRows16 - 1) / kRows16), kWarps * 32, 0, stream>>>(f);
+    else
+      q8_store_fast_kernel<<<grid_for_rows((rows + kFastRows - 1) / kFastRows), kWarps * 32, 0, stream>>>(f);
   } else {
     q8_store_kernel<<<grid_for_rows(rows), kWarps * 32, 0, stream>>>(a);
   }
