@@ -260,11 +260,23 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // GFX906_FA_DECODE_V16PPW2=0 turns it off (tuning override).
   const char* v16p = std::getenv("GFX906_FA_DECODE_V16PPW2");
   const bool v16_two = !(v16p && v16p[0] == '0');
+  const char* nt3p = std::getenv("GFX906_FA_DECODE_NT3PPW2");
+  const bool nt3_two = !(nt3p && nt3p[0] == '0');
   if (d.tr != NWC_TR && (d.tr ? d.nt == 1 && vq8t : mt == 1) && 2 * d.P <= (d.HG == 1 ? MAXP : 8) &&
       need(3, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = 3;
+  } else if (nt3_two && d.tr == NWC && d.nt == 3 && 2 * d.P <= 8 && need(2, 2 * d.P) <= kSmem) {
+    // 17-24 query rows per kv head (4-token speculative verify at GQA 6):
+    // two pages per warp in two stages (three do not fit beside the
+    // shared-memory Q tiles), twice the independent work per warp in the
+    // latency-bound three-n-tile consumer (config 5's verify rows: decode
+    // 1.17 -> 1.01 ms, the mixed step 3.79 -> 3.63 ms);
+    // GFX906_FA_DECODE_NT3PPW2=0 turns it off (tuning override).
+    d.ppw = 2;
+    d.P *= 2;
+    d.nst = 2;
   } else if (v16_two && d.tr == NWC && v16 && d.nt == 1 && d.HG <= 2 && need(2, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;

@@ -1681,7 +1681,9 @@ cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
     }
   } else if constexpr (VT != 2) {
     if (d.tr) {
-      if (d.nt == 3)
+      if (d.nt == 3 && d.ppw == 2)
+        kern = decode_kernel<2, VT, MASK, 2, 2, dec::NWC, 3>;
+      else if (d.nt == 3)
         kern = d.nst == 4 ? decode_kernel<2, VT, MASK, 4, 1, dec::NWC, 3> : decode_kernel<2, VT, MASK, 3, 1, dec::NWC, 3>;
       else
         kern = d.nst == 4 ? decode_kernel<2, VT, MASK, 4, 1, dec::NWC, 2> : decode_kernel<2, VT, MASK, 3, 1, dec::NWC, 2>;
