@@ -25,9 +25,9 @@
 //     TMEM lane i).  Tensor memory: S0 S1 (128 fp32 columns each; P_i is
 //     written as packed fp16 over S_i), O0 O1 (128 columns each).  The MMA
 //     order PV0(j) S0(j+1) PV1(j) S1(j+1) keeps the tensor core on one tile
-//     while the other tile's softmax runs.  Exponentials are split between
-//     MUFU (ex2.approx) and a polynomial on the FMA pipe (one pair in four)
-//     so that neither pipe limits the tensor core.  The running max is
+//     while the other tile's softmax runs.  Exponentials run on MUFU
+//     (ex2.approx), packed arithmetic (f32x2) keeps the softmax's issue
+//     slots few.  The running max is
 //     rescaled lazily (only when it grows by more than 2^8), so O is rarely
 //     touched by the softmax warps.
 //
@@ -377,43 +377,6 @@ __device__ __forceinline__ uint64_t f2add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
-__device__ __forceinline__ uint64_t f2add_rd(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-
-// 2^x for a pair on the FMA pipe, for x <= 2^7 (Cody-Waite split into floor
-// and fraction, then a degree-3 minimax polynomial for 2^f on [0, 1),
-// relative error 7.5e-5, below the fp16 rounding of P).  floor(x) comes from
-// adding 1.5 * 2^23 with round-down, which leaves it in the low mantissa
-// bits; shifting those bits into the exponent field scales the polynomial.
-// Inputs below -126 (including -inf) are clamped to -126: the polynomial lies
-// in [0.99992, 2), so its exponent field stays >= 0 (a denormal at most,
-// which rounds to 0 in fp16) and never borrows into the sign bit.
-__device__ __forceinline__ uint64_t exp2_fma2(uint64_t x2) {
-  float a, b;
-  f2unpack(x2, a, b);
-  x2 = f2pack(fmaxf(a, -126.f), fmaxf(b, -126.f));
-  const uint64_t magic = f2pack(12582912.f, 12582912.f);
-  const uint64_t t = f2add_rd(x2, magic);
-  const uint64_t f = f2sub(x2, f2sub(t, magic));
-  uint64_t p = f2fma(f2pack(0.07802300900220871f, 0.07802300900220871f), f,
-                     f2pack(0.2260693907737732f, 0.2260693907737732f));
-  p = f2fma(p, f, f2pack(0.6958328485488892f, 0.6958328485488892f));
-  p = f2fma(p, f, f2pack(0.9999252557754517f, 0.9999252557754517f));
-  float p0, p1, t0, t1;
-  f2unpack(p, p0, p1);
-  f2unpack(t, t0, t1);
-  return f2pack(__int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23)),
-                __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23)));
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -671,7 +634,11 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
           tmem_st32(tO + lane_off + c * 32, o);
         }
       }
-      // P = 2^(x - m): one pair in four on the FMA pipe, the rest on MUFU
+      // P = 2^(x - m), all on MUFU (ex2.approx).  Moving a share to a
+      // polynomial on the FMA pipe measured slower on the current kernel
+      // (32K prefill: 1/4 of the pairs 1065-1090, 1/8 1131-1146, none
+      // 1147-1172 TFLOP/s): the softmax warps are bound by issue slots, and
+      // the polynomial costs about six per score against one MUFU issue.
       const float mu = m_run == -INFINITY ? 0.f : m_run;
       const float sc = MASK ? 1.f : pp.scale_log2;
       const uint64_t sc2 = f2pack(sc, sc);
@@ -684,14 +651,9 @@ __global__ void __launch_bounds__(pf::NTHREADS, 1) prefill_kernel(const __grid_c
         for (int e = 0; e < 8; ++e) {
           const uint64_t x2 = f2fma(f2pack(__uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e]),
                                            __uint_as_float(s[c >> 1][(c & 1) * 16 + 2 * e + 1])), sc2, nmu2);
-          uint64_t p2;
-          if ((e & 3) == 3) {
-            p2 = exp2_fma2(x2);
-          } else {
-            float x0, x1;
-            f2unpack(x2, x0, x1);
-            p2 = f2pack(fast_exp2(x0), fast_exp2(x1));
-          }
+          float x0, x1;
+          f2unpack(x2, x0, x1);
+          const uint64_t p2 = f2pack(fast_exp2(x0), fast_exp2(x1));
           ls2[e & 1] = f2add(ls2[e & 1], p2);
           float p0, p1;
           f2unpack(p2, p0, p1);
