@@ -258,7 +258,7 @@ DECODE_TRAFFIC_RATIO = {"q8_0": (462.63 + 5.18) / 462.36, "fp16": (666.54 + 5.09
 # DRAM bytes (read + write) per FLOP of prefill_kernel, from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum) of the last 8192-query chunk
 # of the 32K prefill: 1.389 GB + 0.107 GB for 5.773 TFLOP.
-PREFILL_TRAFFIC_PER_FLOP = (1.421075e9 + 0.109067e9) / 5.77253670912e12
+PREFILL_TRAFFIC_PER_FLOP = (1.384802e9 + 0.109156e9) / 5.77253670912e12
 PREFILL_TRAFFIC_NOTE = ("ncu dram read+write of prefill_kernel on the chunk at offset 24576 of config 4 "
                         "(profiles/prefill_kernel_config4_chunk24k.md) per algorithmic FLOP, scaled to this "
                         "workload's FLOPs")
