@@ -262,7 +262,13 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   const bool v16_two = !(v16p && v16p[0] == '0');
   const char* nt3p = std::getenv("GFX906_FA_DECODE_NT3PPW2");
   const bool nt3_two = !(nt3p && nt3p[0] == '0');
-  if (d.tr != NWC_TR && (d.tr ? d.nt == 1 && vq8t : mt == 1) && 2 * d.P <= (d.HG == 1 ? MAXP : 8) &&
+  // 9-16 rows per kv head (two n-tiles, Q^T in registers): two pages per warp
+  // in three stages as for one n-tile (config 3 with two query tokens per
+  // sequence: 8 kv heads 526 -> 468 us, one kv head 87 -> 77.5 us);
+  // GFX906_FA_DECODE_NT2PPW2=0 turns it off (tuning override).
+  const char* nt2p = std::getenv("GFX906_FA_DECODE_NT2PPW2");
+  const bool nt2_two = !(nt2p && nt2p[0] == '0');
+  if (d.tr != NWC_TR && (d.tr ? (d.nt == 1 || (d.nt == 2 && nt2_two)) && vq8t : mt == 1) && 2 * d.P <= (d.HG == 1 ? MAXP : 8) &&
       need(3, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;

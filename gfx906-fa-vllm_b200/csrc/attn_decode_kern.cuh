@@ -1677,6 +1677,7 @@ cudaError_t launch_decode_t(const DecodeParams& d, cudaStream_t stream) {
         if (d.ppw == 2) kern = decode_kernel<1, 3, MASK, 3, 2, dec::NWC>;
       } else if (d.tr) {
         kern = d.nst == 4 ? decode_kernel<1, 3, MASK, 4, 1, dec::NWC, 2> : decode_kernel<1, 3, MASK, 3, 1, dec::NWC, 2>;
+        if (d.ppw == 2) kern = decode_kernel<1, 3, MASK, 3, 2, dec::NWC, 2>;
       }
     }
   } else if constexpr (VT != 2) {
