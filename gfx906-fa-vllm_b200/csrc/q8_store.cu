@@ -43,6 +43,7 @@ struct StoreArgs {
   int v_store_w;                // same for V rows
   int vec_ok_k, vec_ok_v;       // 1 when 4-element vector loads are aligned
   int hkv_log2, bs_log2;        // fast path: log2 of Hkv and block size (powers of two)
+  int k_tok16;                  // fast16 path: a token's 8 Q8_0 K rows are 1088 contiguous, 16-byte aligned bytes
   // fused RoPE (rope_store_kernel only)
   void* query;                  // [T, Hq, D], rotated in place (may be null)
   int q_dt, Hq;
@@ -384,6 +385,18 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast16_kernel(StoreArgs 
         *reinterpret_cast<uint4*>(a.v_cache + vdst[k] + 16 * hl) = vraw[k];
     }
     __syncwarp();
+    if (a.k_tok16) {
+      // eight kv heads: the warp's 8 rows are one token's heads, adjacent in
+      // the cache (1088 bytes, 16-byte aligned): 68 16-byte stores
+      const int64_t kd = kdst_s[0];
+      if (kd >= 0) {
+#pragma unroll
+        for (int it = lane; it < kRows16 * kFastRowBytes / 16; it += 32)
+          reinterpret_cast<uint4*>(a.k_cache + kd)[it] = reinterpret_cast<const uint4*>(stage)[it];
+      }
+      __syncwarp();
+      continue;
+    }
     // the 8 Q8_0 K rows (17 x 8 bytes each) leave as 136 aligned 8-byte stores
 #pragma unroll
     for (int it = lane; it < kRows16 * (kFastRowBytes / 8); it += 32) {
@@ -536,6 +549,8 @@ cudaError_t launch_store(const StoreArgs& a, cudaStream_t stream) {
                      (a.v_mode == G9_V_NONE ||
                       (((uintptr_t)a.value % 16) == 0 &&
                        (((uintptr_t)a.v_cache | (uintptr_t)a.vc_blk | (uintptr_t)a.vc_tok | (uintptr_t)a.vc_head) % 16) == 0));
+    f.k_tok16 = a.Hkv == kRows16 && a.kc_head == kFastRowBytes &&
+                (((uintptr_t)a.k_cache | (uintptr_t)a.kc_blk | (uintptr_t)a.kc_tok) % 16) == 0;
     if (w16)
       q8_store_fast16_kernel<<<grid_for_rows((rows + kRows16 - 1) / kRows16), kWarps * 32, 0, stream>>>(f);
     else
