@@ -318,23 +318,14 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast16_kernel(StoreArgs 
   for (int64_t r0 = ((int64_t)blockIdx.x * kWarps + warp_id()) * kRows16; r0 < rows;
        r0 += (int64_t)gridDim.x * kWarps * kRows16) {
     uint4 kraw[kRows16 / 2], vraw[kRows16 / 2];
-    int64_t kdst[kRows16 / 2], vdst[kRows16 / 2];
+    int64_t slot[kRows16 / 2];          // destinations are derived from the slot where they are used
 #pragma unroll
     for (int k = 0; k < kRows16 / 2; ++k) {
       const int64_t row64 = r0 + 2 * k + half;
       const bool valid = row64 < rows;
       const uint32_t row = (uint32_t)row64;
-      const uint32_t t = row >> a.hkv_log2, h = row & ((1u << a.hkv_log2) - 1);
-      const int64_t s = valid ? (a.slot_mapping ? a.slot_mapping[t] : (int64_t)t) : -1;
-      if (s >= 0) {
-        const uint64_t s64 = (uint64_t)s;
-        const uint32_t blk = (uint32_t)(s64 >> a.bs_log2);
-        const uint32_t off = (uint32_t)s64 & ((1u << a.bs_log2) - 1);
-        kdst[k] = (int64_t)((uint64_t)blk * (uint32_t)a.kc_blk + (off * (uint32_t)a.kc_tok + h * (uint32_t)a.kc_head));
-        vdst[k] = (int64_t)((uint64_t)blk * (uint32_t)a.vc_blk + (off * (uint32_t)a.vc_tok + h * (uint32_t)a.vc_head));
-      } else {
-        kdst[k] = vdst[k] = -1;
-      }
+      const uint32_t t = row >> a.hkv_log2;
+      slot[k] = valid ? (a.slot_mapping ? a.slot_mapping[t] : (int64_t)t) : -1;
       kraw[k] = valid ? reinterpret_cast<const uint4*>(a.key)[(size_t)row * 16 + hl] : make_uint4(0u, 0u, 0u, 0u);
       vraw[k] = (valid && a.v_mode == G9_V_COPY16) ? reinterpret_cast<const uint4*>(a.value)[(size_t)row * 16 + hl]
                                                    : make_uint4(0u, 0u, 0u, 0u);
@@ -380,9 +371,20 @@ __global__ void __launch_bounds__(kWarps * 32) q8_store_fast16_kernel(StoreArgs 
       o16[2] = (uint16_t)(p1 & 0xffffu);
       o16[3] = (uint16_t)(p1 >> 16);
       if ((hl & 3) == 0) *reinterpret_cast<uint16_t*>(out) = __half_as_ushort(__float2half_rn(dq));
-      if (hl == 0) kdst_s[r] = kdst[k];
-      if (a.v_mode == G9_V_COPY16 && vdst[k] >= 0)
-        *reinterpret_cast<uint4*>(a.v_cache + vdst[k] + 16 * hl) = vraw[k];
+      if (slot[k] >= 0) {
+        const uint32_t h = (uint32_t)(r0 + r) & ((1u << a.hkv_log2) - 1);
+        const uint64_t s64 = (uint64_t)slot[k];
+        const uint32_t blk = (uint32_t)(s64 >> a.bs_log2);
+        const uint32_t off = (uint32_t)s64 & ((1u << a.bs_log2) - 1);
+        if (hl == 0)
+          kdst_s[r] = (int64_t)((uint64_t)blk * (uint32_t)a.kc_blk + (off * (uint32_t)a.kc_tok + h * (uint32_t)a.kc_head));
+        if (a.v_mode == G9_V_COPY16)
+          *reinterpret_cast<uint4*>(a.v_cache + (int64_t)((uint64_t)blk * (uint32_t)a.vc_blk +
+                                                          (off * (uint32_t)a.vc_tok + h * (uint32_t)a.vc_head)) +
+                                    16 * hl) = vraw[k];
+      } else if (hl == 0) {
+        kdst_s[r] = -1;
+      }
     }
     __syncwarp();
     if (a.k_tok16) {
