@@ -64,7 +64,9 @@ __device__ __forceinline__ void write_k_rows(const GatherArgs& a, int b, int tok
   }
 }
 
-template <bool kBulk>
+// kFixed: 16-token pages, D = 128 (136-byte K rows, 256-byte V rows) and
+// 8-byte K stores: the write loops index with compile-time divisors.
+template <bool kBulk, bool kFixed = false>
 __global__ void __launch_bounds__(kGatherThreads) gather_kernel(GatherArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
@@ -116,6 +118,24 @@ __global__ void __launch_bounds__(kGatherThreads) gather_kernel(GatherArgs a) {
     }
   }
 
+  if constexpr (kFixed) {
+    // V: 16 tokens x 16 chunks of 16 bytes per head; K: 16 rows x 17 words of 8 bytes per head
+    for (int i = threadIdx.x; i < a.Hkv * 256; i += blockDim.x) {
+      const int h = i >> 8, t = (i >> 4) & 15, c = i & 15;
+      if (t >= ntok) continue;
+      uint4 val = make_uint4(0u, 0u, 0u, 0u);
+      if (t < nvalid) val = *reinterpret_cast<const uint4*>(vsrc + t * v_tok + h * v_head + c * 16);
+      *reinterpret_cast<uint4*>(a.vo + (((int64_t)b * a.Hkv + h) * a.Sk + tok0 + t) * 256 + c * 16) = val;
+    }
+    for (int i = threadIdx.x; i < a.Hkv * 272; i += blockDim.x) {
+      const int h = i / 272, r = i - h * 272;
+      const int t = r / 17, c = r - t * 17;
+      if (t >= nvalid) continue;
+      *reinterpret_cast<uint2*>(a.ko + (((int64_t)b * a.Hkv + h) * a.Sk + tok0 + t) * 136 + c * 8) =
+          *reinterpret_cast<const uint2*>(ksrc + t * k_tok + h * k_head + c * 8);
+    }
+    return;
+  }
   // ---- V: copy valid rows, zero the rest of the page up to Sk -------------
   {
     const int chunks = vrow / 16;                  // 16-byte chunks per row
@@ -188,10 +208,11 @@ extern "C" cudaError_t gfx906_fa_gather_paged_kv_q8_checked(
   dim3 grid((Sk + block_size - 1) / block_size, num_seqs);
   if (bulk) {
     const size_t smem = (size_t)(kbytes + vbytes);
-    cudaError_t e = cudaFuncSetAttribute(gather_kernel<true>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const bool fixed = block_size == 16 && D == 128 && a.kw == 8;
+    auto kern = fixed ? gather_kernel<true, true> : gather_kernel<true, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    gather_kernel<true><<<grid, kGatherThreads, smem, stream>>>(a);
+    kern<<<grid, kGatherThreads, smem, stream>>>(a);
   } else {
     gather_kernel<false><<<grid, kGatherThreads, 0, stream>>>(a);
   }
