@@ -254,9 +254,9 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
   // loads / conversions / MMAs (the kernel is latency-bound), with 3 stages
   // (one m-tile only: with two the registers would spill); else one page per
   // warp with 4 stages, or 3 when 4 do not fit.
-  // 16-bit V rows at one or two kv heads per CTA: two pages per warp too, in
-  // two stages when three do not fit (config 3's two-head share with fp16 V
-  // 177.5 -> 151.8 us, one head 110.7 -> 106.8 us);
+  // 16-bit V rows: two pages per warp too, in two stages when three do not
+  // fit (config 3 with fp16 V: two-head share 177.5 -> 151.8 us, one head
+  // 110.7 -> 106.8 us; four heads 287 -> 249 us, all eight 514 -> 465 us);
   // GFX906_FA_DECODE_V16PPW2=0 turns it off (tuning override).
   const char* v16p = std::getenv("GFX906_FA_DECODE_V16PPW2");
   const bool v16_two = !(v16p && v16p[0] == '0');
@@ -283,7 +283,7 @@ static cudaError_t plan_decode(const G9AttnBatch& p, DecodeParams& d, int& mt) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = 2;
-  } else if (v16_two && d.tr == NWC && v16 && d.nt == 1 && d.HG <= 2 && need(2, 2 * d.P) <= kSmem) {
+  } else if (v16_two && d.tr == NWC && v16 && d.nt == 1 && 2 * d.P <= MAXP && need(2, 2 * d.P) <= kSmem) {
     d.ppw = 2;
     d.P *= 2;
     d.nst = need(3, d.P) <= kSmem ? 3 : 2;
